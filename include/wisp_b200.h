@@ -1,0 +1,132 @@
+/*
+ * wisp_b200.h - C ABI of the B200 paged fused-MoE layer.
+ *
+ * One opaque handle per MoE layer holds what the reference keeps in a
+ * per-layer ``WispMoEState`` (src/wisp/integrations/vllm/fused_moe.py:126-236):
+ * the pinned host masters of the expert weights (caller-owned), the HBM slot
+ * scratch, the expert->slot map, the LRU state and the counters.  The LRU
+ * pager runs on the device, page-in runs on copy-engine streams, expert
+ * compute runs in hand-written sm_100a kernels.
+ *
+ * Conventions
+ *   - every function returns a status (WISP_OK == 0); on failure
+ *     wisp_last_error() gives a message for the calling thread;
+ *   - ``stream`` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream); x / topk_* / out pointers are device pointers;
+ *   - expert weights are bf16: w13 [E][2I][H] (gate rows then up rows), w2
+ *     [E][H][I], like vLLM's UnquantizedFusedMoEMethod.create_weights.
+ */
+#ifndef WISP_B200_H
+#define WISP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WISP_API __attribute__((visibility("default")))
+#else
+#define WISP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct wisp_layer wisp_layer;
+
+enum wisp_status {
+    WISP_OK = 0,
+    WISP_ERR_INVALID = 1,      /* bad argument / shape / unpinned host memory */
+    WISP_ERR_OVERFLOW = 2,     /* one call's unique experts exceed the cap ("sub-batch" error) */
+    WISP_ERR_BAD_EXPERT = 3,   /* routed expert id outside [0, E) */
+    WISP_ERR_CUDA = 4,         /* a CUDA runtime call failed */
+    WISP_ERR_TIMEOUT = 5,      /* a bounded device or host wait ran out */
+    WISP_ERR_NOMEM = 6,        /* device or pinned allocation failed */
+    WISP_ERR_UNSUPPORTED = 7   /* shape/mode not supported by the compute kernels */
+};
+
+enum wisp_mode { WISP_MODE_PAGED = 0, WISP_MODE_RESIDENT = 1 };
+
+/* Library version string and the message of this thread's last failure. */
+WISP_API const char *wisp_version(void);
+WISP_API const char *wisp_last_error(void);
+
+/*
+ * Create a layer.  Replaces WispMoEState.__init__ (fused_moe.py:161-236):
+ * scratch [cap][w13_expert_bytes] and [cap][w2_expert_bytes] in HBM,
+ * expert_map[E] = -1, slot_to_expert[cap] = -1, lru_tick[cap] = 0, clock 0.
+ * host_w13 / host_w2 are the pinned host masters ([E][bytes] each); they
+ * must stay alive and pinned for the layer's lifetime.  hidden / inter give
+ * the bf16 compute shape (0, 0 for a paging-only layer).
+ */
+WISP_API int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden,
+                      int32_t inter, int64_t w13_expert_bytes, int64_t w2_expert_bytes,
+                      const void *host_w13, const void *host_w2, int32_t device,
+                      int32_t mode, wisp_layer **out);
+WISP_API int wisp_layer_destroy(wisp_layer *layer);
+
+/*
+ * Paged MoE forward of ``num_tokens`` rows.  Replaces the pager + compute of
+ * _wisp_forward_cuda_paged (fused_moe.py:1017, 1102-1168) and vLLM
+ * fused_experts with expert_map (called at fused_moe.py:1106-1118, 1155-1167):
+ * first-fit token sub-batching, one LRU step per group (bit-exact with the
+ * reference's ensure_resident), page-in of the misses, gate-up GEMM + SiLU-mul,
+ * down GEMM x routing weight, routing-order combine.
+ *   x [T][H] bf16, topk_weights [T][k] fp32, topk_ids [T][k] int32 or int64
+ *   (ids_int64 != 0), out [T][H] bf16.
+ * Returns WISP_ERR_OVERFLOW when a single token routes to more unique
+ * experts than the cap (the reference raises RuntimeError "...sub-batch...").
+ */
+WISP_API int wisp_moe_forward(wisp_layer *layer, const void *x, const float *topk_weights,
+                     const void *topk_ids, int32_t ids_int64, int32_t num_tokens,
+                     int32_t top_k, void *out, void *stream);
+
+/*
+ * One LRU admission step for an arbitrary id list, with page-in, finished
+ * before returning.  Replaces WispMoEState.ensure_resident
+ * (fused_moe.py:264-358).
+ */
+WISP_API int wisp_ensure_resident(wisp_layer *layer, const void *ids, int32_t ids_int64, int32_t n,
+                         void *stream);
+
+/*
+ * Pager side of one forward without the expert compute: first-fit groups, one
+ * LRU step per group, page-in, finished before returning; writes the slot each
+ * (token, k) read to slots_out (host, [T][k]; may be NULL).  The test and replay
+ * hook for the bookkeeping of _wisp_forward_cuda_paged (fused_moe.py:1017,
+ * 1102-1168).
+ */
+WISP_API int wisp_pager_step(wisp_layer *layer, const void *topk_ids, int32_t ids_int64,
+                             int32_t num_tokens, int32_t top_k, int32_t *slots_out, void *stream);
+
+/* Resident mode: identity map and full copy.  fused_moe.py:242-258 (cap == E). */
+WISP_API int wisp_prime_identity(wisp_layer *layer, void *stream);
+
+/* Hot resize of the slot scratch, clamped to [2, E].  fused_moe.py:439-490. */
+WISP_API int wisp_resize_cap(wisp_layer *layer, int32_t new_cap, void *stream);
+
+/*
+ * Read back the pager state (synchronises the device).  Any pointer may be
+ * NULL.  stats4 = {forward, miss, hits, evict} (fused_moe.py:211-221).
+ */
+WISP_API int wisp_get_state(wisp_layer *layer, int32_t *slot_to_expert, int64_t *lru_tick,
+                   int64_t *clock, int64_t *stats4, int32_t *expert_map, int32_t *cap);
+
+/* Overwrite the four counters (snapshot_expert_stats reset, fused_moe.py:579-593). */
+WISP_API int wisp_set_stats(wisp_layer *layer, const int64_t *stats4);
+
+/* Device addresses of the slot scratch and expert map (for zero-copy views). */
+WISP_API int wisp_layer_buffers(wisp_layer *layer, void **scratch_w13, void **scratch_w2,
+                       void **expert_map);
+
+/*
+ * Counters of the last wisp_moe_forward on this layer (host side, no sync):
+ * {groups, misses, page-in bytes, unique experts summed over groups}.
+ */
+WISP_API int wisp_last_forward_info(wisp_layer *layer, int64_t *info4);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WISP_B200_H */
