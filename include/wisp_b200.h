@@ -125,6 +125,29 @@ WISP_API int wisp_layer_buffers(wisp_layer *layer, void **scratch_w13, void **sc
  */
 WISP_API int wisp_last_forward_info(wisp_layer *layer, int64_t *info4);
 
+/*
+ * Expert compute from slot scratch that allocates nothing (this entry point
+ * has no counterpart in the reference, which always lets vLLM allocate).
+ * For callers that may not call cudaMalloc: plug-ins inside a serving engine
+ * that has reserved the free HBM for its KV cache and hands out only its own
+ * buffers, or decode loops that cannot take cudaMalloc's implicit device
+ * synchronisation.  Runs the decode kernels of wisp_moe_forward on given
+ * slots: x [T][H] bf16, scratch_w13 [num_slots][2I][H] / scratch_w2
+ * [num_slots][H][I] bf16, pair_slots [T][k] int32 (the slot each (t, k)
+ * reads; a slot outside [0, num_slots) contributes zero), topk_weights
+ * [T][k] fp32, out [T][H] bf16.  Intermediates live in one static device
+ * array of about 6.3 MB per GPU, held until exit: T*k <= 128, hidden <= 8192,
+ * inter <= 16384; larger sizes return WISP_ERR_INVALID.  Calls share that
+ * array, so calls that overlap on the GPU race.  The first call on a device
+ * resolves the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.
+ */
+WISP_API int wisp_expert_compute_noalloc(int32_t device, const void *x, const void *scratch_w13,
+                                         const void *scratch_w2, int32_t num_slots,
+                                         const int32_t *pair_slots, const float *topk_weights,
+                                         int32_t num_tokens, int32_t top_k, int32_t hidden,
+                                         int32_t inter, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

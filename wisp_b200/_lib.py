@@ -47,6 +47,8 @@ SIGNATURES = {
     "wisp_layer_buffers": (ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                           ctypes.POINTER(_vp)]),
     "wisp_last_forward_info": (ctypes.c_int, [_vp, _p64]),
+    "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,
+                                                   _c_int32, _c_int32, _c_int32, _c_int32, _vp, _vp]),
 }
 
 
