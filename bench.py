@@ -174,18 +174,23 @@ def run_wisp(args):
     for s in range(args.warmup):
         step(s, x_d, ids_d, w_d, out_d)
     torch.cuda.synchronize()
+    for st in states:
+        st.synchronize()
     before = [st.stats() for st in states]
-    pagein_bytes = 0
+    tel0 = [st.telemetry() for st in states]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
         torch.cuda.synchronize()
         ev0.record()
         for s in range(args.warmup, total):
             step(s, x_d, ids_d, w_d, out_d)
-            pagein_bytes += sum(st.last_forward_info()["pagein_bytes"] for st in states)
         ev1.record()
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
+    for st in states:
+        st.synchronize()
+    tel1 = [st.telemetry() for st in states]
+    pagein_bytes = sum(b["pagein_bytes"] - a["pagein_bytes"] for a, b in zip(tel0, tel1))
     after = [st.stats() for st in states]
     misses = sum(a[1] - b[1] for a, b in zip(after, before))
     hits = sum(a[2] - b[2] for a, b in zip(after, before))
@@ -271,16 +276,16 @@ def resident_phase(args, masters, dev, hbm_peak):
         for layer in range(L):
             states[layer].forward(x, w_d[s, layer], ids_d[s, layer], out=out)
     torch.cuda.synchronize()
-    ubytes = 0
+    u0 = sum(st.telemetry()["unique_experts"] for st in states)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for s in range(args.warmup, args.warmup + args.steps):
         for layer in range(L):
             states[layer].forward(x, w_d[s, layer], ids_d[s, layer], out=out)
-            ubytes += states[layer].last_forward_info()["unique_experts"] * SHAPE.expert_bytes
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
+    ubytes = (sum(st.telemetry()["unique_experts"] for st in states) - u0) * SHAPE.expert_bytes
     gbs = ubytes / (ms * 1e-3) / 1e9
     for st in states:
         st.close()

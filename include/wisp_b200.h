@@ -66,7 +66,8 @@ WISP_API int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t
 WISP_API int wisp_layer_destroy(wisp_layer *layer);
 
 /*
- * Paged MoE forward of ``num_tokens`` rows.  Replaces the pager + compute of
+ * Paged MoE forward of ``num_tokens`` rows, enqueued on ``stream`` (the call
+ * returns before the work runs; see wisp_layer_sync for errors).  Replaces the pager + compute of
  * _wisp_forward_cuda_paged (fused_moe.py:1017, 1102-1168) and vLLM
  * fused_experts with expert_map (called at fused_moe.py:1106-1118, 1155-1167):
  * first-fit token sub-batching, one LRU step per group (bit-exact with the
@@ -120,10 +121,37 @@ WISP_API int wisp_layer_buffers(wisp_layer *layer, void **scratch_w13, void **sc
                        void **expert_map);
 
 /*
- * Counters of the last wisp_moe_forward on this layer (host side, no sync):
- * {groups, misses, page-in bytes, unique experts summed over groups}.
+ * Cumulative telemetry (synchronises the device): {groups run, misses,
+ * page-in bytes, unique experts read summed over groups}.
  */
-WISP_API int wisp_last_forward_info(wisp_layer *layer, int64_t *info4);
+WISP_API int wisp_get_telemetry(wisp_layer *layer, int64_t *out4);
+
+/*
+ * Wait until every forward issued on this layer has finished (kernels and
+ * page-ins) and return the first error any of them hit since the last check
+ * (WISP_OK if none).  wisp_moe_forward returns before its work runs; a
+ * device-side failure (a routed id outside [0, E), a bounded wait that ran
+ * out) is reported by the next wisp_moe_forward or wisp_layer_sync.  After a
+ * timeout the layer restarts cold (no slot resident; clock and counters kept).
+ */
+WISP_API int wisp_layer_sync(wisp_layer *layer);
+
+/*
+ * Tunables: WISP_CFG_ASYNC (1: single-launch forward with asynchronous
+ * page-in, the default; 0: host-synchronous path), WISP_CFG_WAIT_NS (limit of
+ * one device-side wait, default 10 s), WISP_CFG_DROP_PAGEINS (test fault: the
+ * host silently skips the next n page-ins of this layer),
+ * WISP_CFG_TRACE_BUFFER (debug: device address of a uint64 buffer of
+ * 8 + 4 * grid words that the forward kernel fills with %globaltimer
+ * milestones; 0 = off).
+ */
+enum wisp_config_key {
+    WISP_CFG_ASYNC = 1,
+    WISP_CFG_WAIT_NS = 2,
+    WISP_CFG_DROP_PAGEINS = 4,
+    WISP_CFG_TRACE_BUFFER = 5
+};
+WISP_API int wisp_layer_config(wisp_layer *layer, int32_t key, int64_t value);
 
 /*
  * Expert compute from slot scratch that allocates nothing (this entry point

@@ -67,9 +67,7 @@ def test_noalloc_matches_forward_on_two_calls_paged():
         x = torch.randn(T, shape.hidden, generator=g).to(torch.bfloat16).to(DEV)
         w, ids = wl.softmax_topk(torch.randn(T, E, generator=g), K)
         w, ids = w.to(DEV), ids.to(DEV)
-        slots = st.pager_step(ids)                 # pages the routed experts in
-        if st.last_forward_info()["groups"] != 1:
-            pytest.skip("routing did not fit one group")
+        slots = st.pager_step(ids)                 # pages the routed experts in (one group: cap == E)
         ref = st.forward(x, w, ids)                # all hits now: same slots
         out = torch.full_like(x, float("nan"))
         _noalloc(st, x, w, slots.to(DEV).contiguous(), out)

@@ -23,6 +23,11 @@ WISP_ERR_UNSUPPORTED = 7
 MODE_PAGED = 0
 MODE_RESIDENT = 1
 
+CFG_ASYNC = 1
+CFG_WAIT_NS = 2
+CFG_DROP_PAGEINS = 4
+CFG_TRACE_BUFFER = 5
+
 _c_int32 = ctypes.c_int32
 _c_int64 = ctypes.c_int64
 _vp = ctypes.c_void_p
@@ -46,7 +51,9 @@ SIGNATURES = {
     "wisp_set_stats": (ctypes.c_int, [_vp, _p64]),
     "wisp_layer_buffers": (ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                           ctypes.POINTER(_vp)]),
-    "wisp_last_forward_info": (ctypes.c_int, [_vp, _p64]),
+    "wisp_get_telemetry": (ctypes.c_int, [_vp, _p64]),
+    "wisp_layer_sync": (ctypes.c_int, [_vp]),
+    "wisp_layer_config": (ctypes.c_int, [_vp, _c_int32, _c_int64]),
     "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,
                                                    _c_int32, _c_int32, _c_int32, _c_int32, _vp, _vp]),
 }

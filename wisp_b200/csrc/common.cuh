@@ -60,6 +60,19 @@ __device__ __forceinline__ uint4 ld_cached16(const void *p) {
     return __ldg(reinterpret_cast<const uint4 *>(p));
 }
 
+// Coherent 16-byte load cached in L2 only: for data written during the same
+// kernel (by other CTAs or by the copy engine), which the non-coherent
+// read-only path must not serve.
+__device__ __forceinline__ uint4 ld_cg16(const void *p) {
+    return __ldcg(reinterpret_cast<const uint4 *>(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Butterfly sum over the warp; every lane ends with the same value and the
 // pairing order is fixed, so the result is independent of anything but the
 // 32 inputs.

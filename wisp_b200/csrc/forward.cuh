@@ -1,0 +1,30 @@
+// Persistent, cooperative forward kernel (pager + expert compute in one launch).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "decode.cuh"
+#include "pager.cuh"
+
+namespace wisp {
+
+// Grid-barrier words (device, per layer): [0] arrivals, [1] generation,
+// [2] abort flag, [3] sticky kernel status (first error wins; the host clears it).
+enum { kBarArrive = 0, kBarGen = 1, kBarAbort = 2, kBarStatus = 3, kBarWords = 4 };
+
+struct ForwardParams {
+    PagerParams pg;                 // block 0 runs the pager with these
+    GroupCompute gc;                // x, w13, w2, topk_w, act, y, out, counters, K, H, I
+    const uint32_t *slot_ready;     // [cap] generation landed in each slot (copy-stream writes)
+    unsigned int *bar;              // [kBarWords]
+    unsigned long long *done_word;  // mapped host: (seq << 32) | groups finished
+    long long wait_ns;              // limit of any single wait
+    int *status_word;               // mapped host: sticky kernel status, cleared by the host
+    int publish;                    // block 0 publishes the page-in list (paged mode)
+    // optional %globaltimer trace (debug): [0..7] block 0 milestones, then 4 words per block
+    unsigned long long *trace;
+};
+
+int launch_forward(const ForwardParams &p, int max_tokens_per_group, cudaStream_t stream);
+
+}  // namespace wisp

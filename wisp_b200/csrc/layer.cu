@@ -2,27 +2,43 @@
 //
 // A wisp_layer is the B200 counterpart of the reference's WispMoEState
 // (src/wisp/integrations/vllm/fused_moe.py:126-490): slot scratch in HBM,
-// the expert map and LRU state in device memory (updated by the device
-// pager, K1), a copy-engine stream for page-in from the caller's pinned host
-// masters, and the compute kernels (K3).
+// the expert map and LRU state in device memory (owned by the device pager),
+// a copy-engine stream for page-in from the caller's pinned host masters,
+// and the compute kernels.
 //
-// Forward (wisp_moe_forward), per call:
-//   1. K1 on the caller's stream: groups + LRU for every group, page-in list
-//      into a mapped pinned mailbox;
-//   2. the host waits for K1 (one event), reads the mailbox;
-//   3. per group g: the group's page-ins go to the copy stream after the
-//      compute event of the last earlier group of this call that read the
-//      victim slot (write-after-read); the caller's stream waits for the
-//      copies, then runs K3 for the group and records the group's event.
-// Copies of one group overlap the compute of earlier groups whenever the
-// victims were not read by them.
+// Forward, asynchronous path (default when top_k <= cap, i.e. when the
+// working-set overflow of fused_moe.py:313-327 cannot happen):
+//   * one cooperative launch of the persistent forward kernel (forward.cu)
+//     on the caller's stream: pager, then per group gate-up / down / combine;
+//     the host does not wait;
+//   * the per-device page-in engine (a host thread) picks up the call's
+//     page-in list from the mailbox the pager fills (mapped pinned memory,
+//     guarded by a sequence number), and for each miss, once the kernel has
+//     published that the last earlier group reading the victim slot is done,
+//     issues the two H2D copies on the layer's copy stream followed by a
+//     stream memory write of the slot's generation flag, which is what the
+//     kernel waits on before reading the slot.
+// Forward, synchronous path (top_k > cap, or WISP_CFG_ASYNC = 0): the pager
+// kernel runs alone, the host reads the mailbox, issues the page-ins of each
+// group with event ordering and launches the per-group decode kernels.
+// Both paths run the same warp arithmetic (moe_body.cuh), so their outputs are
+// byte-identical.
+#include <cuda.h>
+
 #include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <deque>
+#include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "forward.cuh"
 #include "pager.cuh"
 
 namespace wisp {
@@ -51,13 +67,24 @@ int fail(int code, const std::string &msg) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-__global__ void fill_identity_kernel(int32_t *s2e, int32_t *emap, int n) {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) {
-        s2e[i] = i;
-        emap[i] = i;
-    }
+// cuStreamWriteValue32 through the runtime's driver entry point (no link
+// against libcuda, so the library loads on machines without a driver).
+typedef CUresult (*WriteValue32Fn)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+WriteValue32Fn g_write32 = nullptr;
+std::once_flag g_write32_once;
+
+void init_write32() {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn)
+        g_write32 = reinterpret_cast<WriteValue32Fn>(fn);
+    else
+        cudaGetLastError();
 }
+
+constexpr long long kDefaultWaitNs = 10LL * 1000 * 1000 * 1000;
+constexpr int kMbRing = 4;
 
 }  // namespace
 }  // namespace wisp
@@ -71,35 +98,225 @@ struct wisp_layer {
     char *d13 = nullptr, *d2 = nullptr;
     int32_t *d_s2e = nullptr, *d_emap = nullptr;
     int64_t *d_tick = nullptr, *d_hdr = nullptr;
+    uint32_t *d_slot_gen = nullptr, *d_slot_ready = nullptr;
+    unsigned int *d_bar = nullptr;
     // per-call workspace, grown on demand
     int wsT = -1, wsK = 0;
-    int32_t *d_slots = nullptr, *d_grp_start = nullptr, *d_grp_nu = nullptr, *d_u_slot = nullptr,
-            *d_u_off = nullptr, *d_u_pairs = nullptr, *d_counters = nullptr;
+    int32_t *d_slots = nullptr, *d_grp_start = nullptr, *d_grp_nu = nullptr, *d_grp_nhit = nullptr,
+            *d_u_slot = nullptr, *d_u_gen = nullptr, *d_u_off = nullptr, *d_u_pairs = nullptr,
+            *d_counters = nullptr, *d_dev_hdr = nullptr;
     __nv_bfloat16 *d_act = nullptr, *d_y = nullptr;
-    int32_t *h_mb = nullptr, *d_mb = nullptr;
+    int32_t *h_mb = nullptr, *d_mb = nullptr;  // kMbRing mailboxes of mb_words words
     long mb_words = 0;
+    int mb_next = 0;
+    std::atomic<int> mb_busy[4];                // a page-in task still reads this mailbox
+    int32_t *h_status = nullptr, *d_status = nullptr;  // sticky forward-kernel status (mapped)
+    unsigned long long *h_done = nullptr, *d_done = nullptr;
+    uint32_t *h_flag_ring = nullptr;  // pinned sources of flag copies when stream writes are missing
+    std::atomic<uint32_t> flag_idx{0};
     cudaStream_t copy_stream = nullptr;
-    cudaEvent_t ev_pager = nullptr, ev_copies = nullptr;
+    cudaEvent_t ev_pager = nullptr, ev_copies = nullptr, ev_last = nullptr;
     std::vector<cudaEvent_t> ev_group, ev_copy;
-    int64_t info[4] = {0, 0, 0, 0};
+    uint32_t seq = 0;
+    bool async = true;
+    long long wait_ns = kDefaultWaitNs;
+    unsigned long long *trace = nullptr;  // debug: device buffer for forward-kernel timestamps
+    std::atomic<int> drop_pageins{0};
+    std::atomic<int> host_status{0};
+    std::atomic<int> pending{0};  // page-in tasks queued for this layer
     std::mutex mu;
 };
 
 namespace {
 
+constexpr int kFlagRing = 1 << 16;
+
+// ---------------------------------------------------------------------------
+// Page-in issue (both paths): two H2D copies, then the slot's generation flag.
+// ---------------------------------------------------------------------------
+int issue_pagein(wisp_layer *L, int64_t e, int64_t s, uint32_t gen) {
+    WISP_CUDA_TRY(cudaMemcpyAsync(L->d13 + s * L->b13, L->h13 + e * L->b13, L->b13,
+                                  cudaMemcpyHostToDevice, L->copy_stream));
+    WISP_CUDA_TRY(cudaMemcpyAsync(L->d2 + s * L->b2, L->h2 + e * L->b2, L->b2, cudaMemcpyHostToDevice,
+                                  L->copy_stream));
+    if (g_write32) {
+        CUresult r = g_write32(reinterpret_cast<CUstream>(L->copy_stream),
+                               reinterpret_cast<CUdeviceptr>(L->d_slot_ready + s), gen, 0);
+        if (r == CUDA_SUCCESS) return WISP_OK;
+    }
+    // fallback: a 4-byte copy from a pinned ring, ordered after the weights
+    uint32_t *src = L->h_flag_ring + (L->flag_idx.fetch_add(1) % kFlagRing);
+    *src = gen;
+    WISP_CUDA_TRY(cudaMemcpyAsync(L->d_slot_ready + s, src, sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                  L->copy_stream));
+    return WISP_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Page-in engine: one host thread per device serving every layer's async
+// forwards.  A task is one forward; tasks of one layer are served in order,
+// tasks of different layers independently.
+// ---------------------------------------------------------------------------
+struct PageTask {
+    wisp_layer *L;
+    uint32_t seq;
+    int T;
+    int slot;  // mailbox of this forward
+    bool loaded = false;
+    int nmiss = 0, next = 0;
+    std::vector<int32_t> recs;
+    std::chrono::steady_clock::time_point last;
+};
+
+class Engine {
+  public:
+    explicit Engine(int dev) : dev_(dev) {
+        th_ = std::thread([this] { run(); });
+        th_.detach();
+    }
+
+    void submit(wisp_layer *L, uint32_t seq, int T, int slot) {
+        auto t = std::make_unique<PageTask>();
+        t->L = L;
+        t->seq = seq;
+        t->T = T;
+        t->slot = slot;
+        t->last = std::chrono::steady_clock::now();
+        L->pending.fetch_add(1);
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            q_.push_back(std::move(t));
+        }
+        cv_.notify_one();
+    }
+
+    // Wait until no task of L is queued (bounded).
+    bool wait_idle(wisp_layer *L, long long limit_ns) {
+        auto t0 = std::chrono::steady_clock::now();
+        while (L->pending.load() > 0) {
+            if (std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0)
+                    .count() > limit_ns)
+                return false;
+            std::this_thread::yield();
+        }
+        return true;
+    }
+
+  private:
+    // 0: nothing to do yet, 1: progressed, 2: finished
+    int step(PageTask &t) {
+        wisp_layer *L = t.L;
+        volatile int32_t *mb = L->h_mb + (long)t.slot * L->mb_words;
+        const auto now = std::chrono::steady_clock::now();
+        const long long host_limit = L->wait_ns + 5LL * 1000 * 1000 * 1000;
+        auto timed_out = [&] {
+            return std::chrono::duration_cast<std::chrono::nanoseconds>(now - t.last).count() > host_limit;
+        };
+        auto give_up = [&](int code) {
+            int z = 0;
+            L->host_status.compare_exchange_strong(z, code);
+            return 2;
+        };
+        if (*reinterpret_cast<volatile int32_t *>(L->h_status) != 0) return 2;  // the kernel gave up
+        if (!t.loaded) {
+            if ((uint32_t)mb[7] != t.seq) return timed_out() ? give_up(WISP_ERR_TIMEOUT) : 0;
+            std::atomic_thread_fence(std::memory_order_acquire);
+            const int status = mb[0];
+            const int nmiss = mb[2];
+            if (status != WISP_OK || nmiss == 0) return 2;
+            const long off = mailbox_miss_offset(t.T);
+            t.recs.resize((size_t)nmiss * kMbRec);
+            for (size_t i = 0; i < t.recs.size(); ++i) t.recs[i] = mb[off + (long)i];
+            t.nmiss = nmiss;
+            t.loaded = true;
+            t.last = now;
+        }
+        int progressed = 0;
+        while (t.next < t.nmiss) {
+            const int32_t *rec = t.recs.data() + (size_t)kMbRec * t.next;
+            const int wg = rec[3];
+            if (wg >= 0) {
+                const unsigned long long need = ((unsigned long long)t.seq << 32) | (unsigned)(wg + 1);
+                const unsigned long long have = *reinterpret_cast<volatile unsigned long long *>(L->h_done);
+                if (have < need) return timed_out() ? give_up(WISP_ERR_TIMEOUT) : progressed;
+            }
+            if (L->drop_pageins.load() > 0) {
+                L->drop_pageins.fetch_sub(1);  // test fault: this slot's flag is never raised
+            } else if (issue_pagein(L, rec[0], rec[1], (uint32_t)rec[4]) != WISP_OK) {
+                return give_up(WISP_ERR_CUDA);
+            }
+            ++t.next;
+            t.last = now;
+            progressed = 1;
+        }
+        return 2;
+    }
+
+    void run() {
+        cudaSetDevice(dev_);
+        std::call_once(g_write32_once, init_write32);
+        std::vector<PageTask *> snap, done;
+        std::vector<wisp_layer *> seen;
+        for (;;) {
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return !q_.empty(); });
+                snap.clear();
+                for (auto &p : q_) snap.push_back(p.get());
+            }
+            bool progress = false;
+            seen.clear();
+            done.clear();
+            for (PageTask *t : snap) {
+                if (std::find(seen.begin(), seen.end(), t->L) != seen.end()) continue;
+                seen.push_back(t->L);
+                const int r = step(*t);
+                if (r) progress = true;
+                if (r == 2) done.push_back(t);
+            }
+            if (!done.empty()) {
+                std::lock_guard<std::mutex> lk(mu_);
+                for (PageTask *t : done) {
+                    wisp_layer *L = t->L;
+                    L->mb_busy[t->slot].store(0);
+                    auto it = std::find_if(q_.begin(), q_.end(), [&](const std::unique_ptr<PageTask> &p) {
+                        return p.get() == t;
+                    });
+                    q_.erase(it);
+                    L->pending.fetch_sub(1);
+                }
+            }
+            if (!progress) std::this_thread::yield();
+        }
+    }
+
+    int dev_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    std::deque<std::unique_ptr<PageTask>> q_;
+    std::thread th_;
+};
+
+Engine *engine_for(int dev) {
+    static std::mutex mu;
+    static Engine *engines[64] = {};
+    std::lock_guard<std::mutex> lk(mu);
+    if (!engines[dev]) engines[dev] = new Engine(dev);  // lives until process exit
+    return engines[dev];
+}
+
+// ---------------------------------------------------------------------------
+// allocation helpers
+// ---------------------------------------------------------------------------
 void free_ws(wisp_layer *L) {
-    cudaFree(L->d_slots);
-    cudaFree(L->d_grp_start);
-    cudaFree(L->d_grp_nu);
-    cudaFree(L->d_u_slot);
-    cudaFree(L->d_u_off);
-    cudaFree(L->d_u_pairs);
-    cudaFree(L->d_counters);
-    cudaFree(L->d_act);
-    cudaFree(L->d_y);
+    for (void *p : {(void *)L->d_slots, (void *)L->d_grp_start, (void *)L->d_grp_nu,
+                    (void *)L->d_grp_nhit, (void *)L->d_u_slot,
+                    (void *)L->d_u_gen, (void *)L->d_u_off, (void *)L->d_u_pairs, (void *)L->d_counters,
+                    (void *)L->d_dev_hdr, (void *)L->d_act, (void *)L->d_y})
+        cudaFree(p);
     if (L->h_mb) cudaFreeHost(L->h_mb);
-    L->d_slots = L->d_grp_start = L->d_grp_nu = L->d_u_slot = L->d_u_off = L->d_u_pairs =
-        L->d_counters = nullptr;
+    L->d_slots = L->d_grp_start = L->d_grp_nu = L->d_grp_nhit = L->d_u_slot = L->d_u_gen = L->d_u_off =
+        L->d_u_pairs = L->d_counters = L->d_dev_hdr = nullptr;
     L->d_act = L->d_y = nullptr;
     L->h_mb = L->d_mb = nullptr;
     L->wsT = -1;
@@ -108,25 +325,30 @@ void free_ws(wisp_layer *L) {
 
 int ensure_ws(wisp_layer *L, int T, int K) {
     if (T <= L->wsT && K <= L->wsK) return WISP_OK;
-    int nT = std::max(T, std::max(L->wsT, 16)), nK = std::max(K, L->wsK);
+    int nT = std::max(T, std::max(L->wsT, 16)), nK = std::max(K, std::max(L->wsK, 8));
     free_ws(L);
-    const size_t P = (size_t)nT * nK;
-    WISP_CUDA_TRY(cudaMalloc(&L->d_slots, sizeof(int32_t) * std::max<size_t>(P, 1)));
+    const size_t P = std::max<size_t>((size_t)nT * nK, 1);
+    WISP_CUDA_TRY(cudaMalloc(&L->d_slots, sizeof(int32_t) * P));
     WISP_CUDA_TRY(cudaMalloc(&L->d_grp_start, sizeof(int32_t) * (nT + 1)));
     WISP_CUDA_TRY(cudaMalloc(&L->d_grp_nu, sizeof(int32_t) * (nT + 1)));
-    WISP_CUDA_TRY(cudaMalloc(&L->d_u_slot, sizeof(int32_t) * std::max<size_t>(P, 1)));
+    WISP_CUDA_TRY(cudaMalloc(&L->d_grp_nhit, sizeof(int32_t) * (nT + 1)));
+    WISP_CUDA_TRY(cudaMalloc(&L->d_u_slot, sizeof(int32_t) * P));
+    WISP_CUDA_TRY(cudaMalloc(&L->d_u_gen, sizeof(int32_t) * P));
     WISP_CUDA_TRY(cudaMalloc(&L->d_u_off, sizeof(int32_t) * (P + nT + 1)));
-    WISP_CUDA_TRY(cudaMalloc(&L->d_u_pairs, sizeof(int32_t) * std::max<size_t>(P, 1)));
+    WISP_CUDA_TRY(cudaMalloc(&L->d_u_pairs, sizeof(int32_t) * P));
+    WISP_CUDA_TRY(cudaMalloc(&L->d_dev_hdr, sizeof(int32_t) * kHdrWords));
     const int H = std::max(L->H, 8), I = std::max(L->I, 8);
-    const int nblk = (H + 7) / 8;
+    const int nblk = (H + 3) / 4;  // row quads (forward kernel) >= row octets (decode kernels)
     WISP_CUDA_TRY(cudaMalloc(&L->d_counters, sizeof(int32_t) * nblk));
     WISP_CUDA_TRY(cudaMemset(L->d_counters, 0, sizeof(int32_t) * nblk));
     if (L->H > 0 && L->I > 0) {
-        WISP_CUDA_TRY(cudaMalloc(&L->d_act, sizeof(__nv_bfloat16) * std::max<size_t>(P, 1) * I));
-        WISP_CUDA_TRY(cudaMalloc(&L->d_y, sizeof(__nv_bfloat16) * std::max<size_t>(P, 1) * H));
+        WISP_CUDA_TRY(cudaMalloc(&L->d_act, sizeof(__nv_bfloat16) * P * I));
+        WISP_CUDA_TRY(cudaMalloc(&L->d_y, sizeof(__nv_bfloat16) * P * H));
     }
-    L->mb_words = mailbox_words(nT, nK);
-    WISP_CUDA_TRY(cudaHostAlloc(&L->h_mb, sizeof(int32_t) * L->mb_words, cudaHostAllocMapped));
+    const long words = (mailbox_words(nT, nK) + 31) & ~31L;
+    WISP_CUDA_TRY(cudaHostAlloc(&L->h_mb, sizeof(int32_t) * words * kMbRing, cudaHostAllocMapped));
+    std::fill(L->h_mb, L->h_mb + words * kMbRing, 0);
+    L->mb_words = words;
     WISP_CUDA_TRY(cudaHostGetDevicePointer((void **)&L->d_mb, L->h_mb, 0));
     L->wsT = nT;
     L->wsK = nK;
@@ -144,22 +366,23 @@ int ensure_events(wisp_layer *L, int G) {
     return WISP_OK;
 }
 
-int alloc_state(wisp_layer *L, int cap) {
+int alloc_slots(wisp_layer *L, int cap) {
     WISP_CUDA_TRY(cudaMalloc(&L->d13, (size_t)cap * L->b13));
     WISP_CUDA_TRY(cudaMalloc(&L->d2, (size_t)cap * L->b2));
     WISP_CUDA_TRY(cudaMalloc(&L->d_s2e, sizeof(int32_t) * cap));
     WISP_CUDA_TRY(cudaMalloc(&L->d_tick, sizeof(int64_t) * cap));
+    WISP_CUDA_TRY(cudaMalloc(&L->d_slot_gen, sizeof(uint32_t) * cap));
+    WISP_CUDA_TRY(cudaMalloc(&L->d_slot_ready, sizeof(uint32_t) * cap));
     WISP_CUDA_TRY(cudaMemset(L->d_s2e, 0xff, sizeof(int32_t) * cap));
     WISP_CUDA_TRY(cudaMemset(L->d_tick, 0, sizeof(int64_t) * cap));
+    WISP_CUDA_TRY(cudaMemset(L->d_slot_gen, 0, sizeof(uint32_t) * cap));
+    WISP_CUDA_TRY(cudaMemset(L->d_slot_ready, 0, sizeof(uint32_t) * cap));
     return WISP_OK;
 }
 
-// Run K1 and wait for it; returns the pager status.
-int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int single_group,
-              int count_forward, cudaStream_t stream) {
-    int rc = ensure_ws(L, T, K);
-    if (rc) return rc;
-    PagerParams p{};
+void fill_pager_params(wisp_layer *L, PagerParams &p, const void *ids, int ids64, int T, int K,
+                       int single_group, int count_forward) {
+    p = PagerParams{};
     p.ids = ids;
     p.ids64 = ids64;
     p.T = T;
@@ -169,18 +392,85 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
     p.mode = L->mode;
     p.count_forward = count_forward;
     p.single_group = single_group;
+    if (++L->seq == 0) ++L->seq;  // 0 marks a mailbox being rewritten
+    p.seq = L->seq;
     p.s2e = L->d_s2e;
     p.tick = L->d_tick;
     p.emap = L->d_emap;
     p.hdr = L->d_hdr;
+    p.slot_gen = L->d_slot_gen;
     p.slots = L->d_slots;
     p.grp_start = L->d_grp_start;
     p.grp_nu = L->d_grp_nu;
+    p.grp_nhit = L->d_grp_nhit;
     p.u_slot = L->d_u_slot;
+    p.u_gen = L->d_u_gen;
     p.u_off = L->d_u_off;
     p.u_pairs = L->d_u_pairs;
+    p.dev_hdr = L->d_dev_hdr;
     p.mb = L->d_mb;
-    L->h_mb[0] = -1;
+}
+
+// Wait for every async forward of L (kernels and page-ins).
+int drain(wisp_layer *L) {
+    WISP_CUDA_TRY(cudaEventSynchronize(L->ev_last));
+    if (!engine_for(L->dev)->wait_idle(L, L->wait_ns + 10LL * 1000 * 1000 * 1000))
+        return fail(WISP_ERR_TIMEOUT, "wisp: page-in engine did not drain");
+    WISP_CUDA_TRY(cudaStreamSynchronize(L->copy_stream));
+    return WISP_OK;
+}
+
+// Restart the pager cold after a failed forward: no slot resident, the
+// grid-barrier words and slot flags consistent again; clock and counters kept.
+int reset_cold(wisp_layer *L) {
+    WISP_CUDA_TRY(cudaDeviceSynchronize());
+    WISP_CUDA_TRY(cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords));
+    WISP_CUDA_TRY(cudaMemset(L->d_s2e, 0xff, sizeof(int32_t) * L->cap));
+    WISP_CUDA_TRY(cudaMemset(L->d_emap, 0xff, sizeof(int32_t) * L->E));
+    WISP_CUDA_TRY(cudaMemset(L->d_tick, 0, sizeof(int64_t) * L->cap));
+    WISP_CUDA_TRY(cudaMemcpy(L->d_slot_ready, L->d_slot_gen, sizeof(uint32_t) * L->cap,
+                             cudaMemcpyDeviceToDevice));
+    const int nblk = (std::max(L->H, 8) + 3) / 4;
+    WISP_CUDA_TRY(cudaMemset(L->d_counters, 0, sizeof(int32_t) * nblk));
+    WISP_CUDA_TRY(cudaDeviceSynchronize());
+    return WISP_OK;
+}
+
+// Errors of earlier async forwards (device sticky status, page-in engine).
+int take_errors(wisp_layer *L) {
+    volatile int32_t *stw = L->h_status;
+    const int dev_st = *stw;
+    const int host_st = L->host_status.exchange(0);
+    if (!dev_st && !host_st) return WISP_OK;
+    const int code = dev_st ? dev_st : host_st;
+    const int rc = drain(L);
+    *stw = 0;
+    if (code == WISP_ERR_BAD_EXPERT) {
+        // the pager rejected the ids before touching any state
+        if (!rc) {
+            cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords);
+            cudaDeviceSynchronize();
+        }
+        return fail(code, "wisp: an earlier forward routed an expert id outside [0, " +
+                              std::to_string(L->E) + ")");
+    }
+    reset_cold(L);
+    return fail(code, code == WISP_ERR_TIMEOUT
+                          ? "wisp: an earlier forward gave up waiting (page-in or grid barrier ran past "
+                            "the wait limit); the layer restarted with no expert resident"
+                          : "wisp: an earlier forward's page-in failed; the layer restarted with no "
+                            "expert resident");
+}
+
+// Run K1 alone and wait for it; returns the pager status (synchronous path).
+int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int single_group,
+              int count_forward, cudaStream_t stream) {
+    int rc = drain(L);
+    if (rc) return rc;
+    rc = ensure_ws(L, T, K);
+    if (rc) return rc;
+    PagerParams p;
+    fill_pager_params(L, p, ids, ids64, T, K, single_group, count_forward);
     WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
     rc = launch_pager(p, stream);
     if (rc) return rc;
@@ -191,7 +481,7 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
         return fail(WISP_ERR_OVERFLOW,
                     "wisp: per-kernel-call working set exceeds cap_experts (" +
                         std::to_string(L->cap) +
-                        "); a single token routes to more unique experts than the cap, so the "
+                        "); a single call routes to more unique experts than the cap, so the "
                         "forward cannot sub-batch it");
     if (status == WISP_ERR_BAD_EXPERT)
         return fail(WISP_ERR_BAD_EXPERT,
@@ -200,8 +490,8 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
     return WISP_OK;
 }
 
-// Issue the page-ins of the mailbox's groups [g0, g1) and, when `compute` is
-// set, the compute of each group.  `stream` is the caller's stream.
+// Synchronous path after run_pager: page-ins per group (write-after-read via
+// group events) and, when `compute` is set, the per-group decode kernels.
 int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K, void *out,
                      cudaStream_t stream, bool compute) {
     const int32_t *mb = L->h_mb;
@@ -212,27 +502,22 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
     int rc = ensure_events(L, std::max(G, 1));
     if (rc) return rc;
     int mi = 0;
-    int64_t utot = 0;
     for (int g = 0; g < G; ++g) {
         const int t0 = grp[g], t1 = grp[g + 1];
         int wait_g = -1, m0 = mi;
-        while (mi < nmiss && rec[4 * mi + 2] == g) {
-            wait_g = std::max(wait_g, (int)rec[4 * mi + 3]);
+        while (mi < nmiss && rec[kMbRec * mi + 2] == g) {
+            wait_g = std::max(wait_g, (int)rec[kMbRec * mi + 3]);
             ++mi;
         }
         if (mi > m0) {
             if (wait_g >= 0) WISP_CUDA_TRY(cudaStreamWaitEvent(L->copy_stream, L->ev_group[wait_g], 0));
             for (int m = m0; m < mi; ++m) {
-                const int64_t e = rec[4 * m], s = rec[4 * m + 1];
-                WISP_CUDA_TRY(cudaMemcpyAsync(L->d13 + s * L->b13, L->h13 + e * L->b13, L->b13,
-                                              cudaMemcpyHostToDevice, L->copy_stream));
-                WISP_CUDA_TRY(cudaMemcpyAsync(L->d2 + s * L->b2, L->h2 + e * L->b2, L->b2,
-                                              cudaMemcpyHostToDevice, L->copy_stream));
+                rc = issue_pagein(L, rec[kMbRec * m], rec[kMbRec * m + 1], (uint32_t)rec[kMbRec * m + 4]);
+                if (rc) return rc;
             }
             WISP_CUDA_TRY(cudaEventRecord(L->ev_copy[g], L->copy_stream));
             WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copy[g], 0));
         }
-        utot += nu[g];
         if (compute && t1 > t0 && nu[g] > 0) {
             const int64_t p0 = (int64_t)t0 * K;
             GroupCompute gc{};
@@ -259,10 +544,62 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
         WISP_CUDA_TRY(cudaEventRecord(L->ev_group[g], stream));
     }
     WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
-    L->info[0] = G;
-    L->info[1] = nmiss;
-    L->info[2] = (int64_t)nmiss * (L->b13 + L->b2);
-    L->info[3] = utot;
+    WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
+    return WISP_OK;
+}
+
+int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids, int ids64, int T,
+                  int K, void *out, cudaStream_t stream) {
+    if (T > L->wsT || K > L->wsK) {
+        int rc = drain(L);
+        if (rc) return rc;
+        rc = ensure_ws(L, T, K);
+        if (rc) return rc;
+    }
+    ForwardParams fp{};
+    fill_pager_params(L, fp.pg, ids, ids64, T, K, 0, 1);
+    fp.gc.x = reinterpret_cast<const __nv_bfloat16 *>(x);
+    fp.gc.w13 = reinterpret_cast<const __nv_bfloat16 *>(L->d13);
+    fp.gc.w2 = reinterpret_cast<const __nv_bfloat16 *>(L->d2);
+    fp.gc.topk_w = w;
+    fp.gc.act = L->d_act;
+    fp.gc.y = L->d_y;
+    fp.gc.out = reinterpret_cast<__nv_bfloat16 *>(out);
+    fp.gc.counters = L->d_counters;
+    fp.gc.K = K;
+    fp.gc.H = L->H;
+    fp.gc.I = L->I;
+    fp.slot_ready = L->d_slot_ready;
+    fp.bar = L->d_bar;
+    fp.done_word = L->d_done;
+    fp.wait_ns = L->wait_ns;
+    fp.status_word = L->d_status;
+    fp.trace = L->trace;
+    const bool paged = L->mode == WISP_MODE_PAGED;
+    fp.publish = paged ? 1 : 0;
+    int slot = 0;
+    if (paged) {
+        // a mailbox no page-in task still reads (the engine frees them in order)
+        slot = L->mb_next;
+        L->mb_next = (slot + 1) % kMbRing;
+        const auto t0 = std::chrono::steady_clock::now();
+        while (L->mb_busy[slot].load()) {
+            if (std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0)
+                    .count() > L->wait_ns + 5LL * 1000 * 1000 * 1000)
+                return fail(WISP_ERR_TIMEOUT, "wisp: page-in engine stalled (mailbox still in use)");
+            std::this_thread::yield();
+        }
+        L->mb_busy[slot].store(1);
+    }
+    fp.pg.mb = L->d_mb + (long)slot * L->mb_words;
+    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
+    int rc = launch_forward(fp, T, stream);
+    if (rc) {
+        if (paged) L->mb_busy[slot].store(0);
+        return rc;
+    }
+    WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
+    if (paged) engine_for(L->dev)->submit(L, fp.pg.seq, T, slot);
     return WISP_OK;
 }
 
@@ -270,7 +607,7 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
 
 extern "C" {
 
-const char *wisp_version(void) { return "wisp_b200 0.1.0 (sm_100a)"; }
+const char *wisp_version(void) { return "wisp_b200 0.2.0 (sm_100a)"; }
 
 const char *wisp_last_error(void) { return g_last_error.c_str(); }
 
@@ -283,14 +620,13 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
         return fail(WISP_ERR_INVALID, "wisp_layer_create: num_experts must be in [1, 1024]");
     if (cap_experts < 1 || cap_experts > num_experts)
         return fail(WISP_ERR_INVALID, "wisp_layer_create: cap_experts must be in [1, num_experts]");
-    if (mode == WISP_MODE_RESIDENT && cap_experts != num_experts)
-        return fail(WISP_ERR_INVALID, "wisp_layer_create: resident mode needs cap == num_experts");
     if (mode != WISP_MODE_PAGED && mode != WISP_MODE_RESIDENT)
         return fail(WISP_ERR_INVALID, "wisp_layer_create: unknown mode");
+    if (mode == WISP_MODE_RESIDENT && cap_experts != num_experts)
+        return fail(WISP_ERR_INVALID, "wisp_layer_create: resident mode needs cap == num_experts");
     if (w13_expert_bytes <= 0 || w2_expert_bytes <= 0 || !host_w13 || !host_w2)
         return fail(WISP_ERR_INVALID, "wisp_layer_create: empty expert weights");
-    if (hidden < 0 || inter < 0)
-        return fail(WISP_ERR_INVALID, "wisp_layer_create: negative shape");
+    if (hidden < 0 || inter < 0) return fail(WISP_ERR_INVALID, "wisp_layer_create: negative shape");
     if (hidden > 0 && inter > 0) {
         if (hidden % 8 || inter % 8)
             return fail(WISP_ERR_UNSUPPORTED, "wisp_layer_create: hidden and inter must be multiples of 8");
@@ -298,7 +634,9 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
             return fail(WISP_ERR_INVALID,
                         "wisp_layer_create: expert bytes do not match bf16 [2I,H] / [H,I]");
     }
+    if (device < 0 || device >= 64) return fail(WISP_ERR_INVALID, "wisp_layer_create: bad device");
     DeviceGuard guard(device);
+    std::call_once(g_write32_once, init_write32);
     cudaPointerAttributes pa{};
     for (const void *hp : {host_w13, host_w2}) {
         if (cudaPointerGetAttributes(&pa, hp) != cudaSuccess || pa.type != cudaMemoryTypeHost) {
@@ -321,22 +659,34 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
         wisp_layer_destroy(L);
         return rc;
     };
-    int rc = alloc_state(L, cap_experts);
-    if (rc) return bail(rc == WISP_ERR_CUDA ? WISP_ERR_NOMEM : rc);
+    if (alloc_slots(L, cap_experts))
+        return bail(fail(WISP_ERR_NOMEM, "wisp_layer_create: HBM allocation failed"));
     if (cudaMalloc(&L->d_emap, sizeof(int32_t) * num_experts) != cudaSuccess ||
-        cudaMalloc(&L->d_hdr, sizeof(int64_t) * 8) != cudaSuccess)
+        cudaMalloc(&L->d_hdr, sizeof(int64_t) * 8) != cudaSuccess ||
+        cudaMalloc(&L->d_bar, sizeof(unsigned int) * kBarWords) != cudaSuccess)
         return bail(fail(WISP_ERR_NOMEM, "wisp_layer_create: device allocation failed"));
     if (cudaMemset(L->d_emap, 0xff, sizeof(int32_t) * num_experts) != cudaSuccess ||
         cudaMemset(L->d_hdr, 0, sizeof(int64_t) * 8) != cudaSuccess ||
+        cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords) != cudaSuccess ||
+        cudaHostAlloc(&L->h_done, sizeof(unsigned long long), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer((void **)&L->d_done, L->h_done, 0) != cudaSuccess ||
+        cudaHostAlloc(&L->h_status, sizeof(int32_t), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer((void **)&L->d_status, L->h_status, 0) != cudaSuccess ||
+        cudaHostAlloc(&L->h_flag_ring, sizeof(uint32_t) * kFlagRing, cudaHostAllocDefault) != cudaSuccess ||
         cudaStreamCreateWithFlags(&L->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&L->ev_pager, cudaEventDisableTiming) !=
-            cudaSuccess ||
-        cudaEventCreateWithFlags(&L->ev_copies, cudaEventDisableTiming) != cudaSuccess)
-        return bail(fail(WISP_ERR_CUDA, "wisp_layer_create: stream/event setup failed"));
-    rc = ensure_ws(L, 16, 8);
+        cudaEventCreateWithFlags(&L->ev_pager, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&L->ev_copies, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&L->ev_last, cudaEventDisableTiming) != cudaSuccess)
+        return bail(fail(WISP_ERR_CUDA, "wisp_layer_create: buffer/stream/event setup failed"));
+    *L->h_done = 0;
+    *L->h_status = 0;
+    for (auto &b : L->mb_busy) b.store(0);
+    int rc = ensure_ws(L, 16, 8);
     if (rc) return bail(rc);
     if (cudaDeviceSynchronize() != cudaSuccess)
         return bail(fail(WISP_ERR_CUDA, "wisp_layer_create: device sync failed"));
+    const char *env = getenv("WISP_B200_SYNC");
+    if (env && env[0] == '1') L->async = false;
     *out = L;
     return WISP_OK;
 }
@@ -344,18 +694,19 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
 int wisp_layer_destroy(wisp_layer *L) {
     if (!L) return WISP_OK;
     DeviceGuard guard(L->dev);
+    if (L->ev_last) drain(L);
     cudaDeviceSynchronize();
     free_ws(L);
-    cudaFree(L->d13);
-    cudaFree(L->d2);
-    cudaFree(L->d_s2e);
-    cudaFree(L->d_tick);
-    cudaFree(L->d_emap);
-    cudaFree(L->d_hdr);
+    for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->d_s2e, (void *)L->d_tick, (void *)L->d_emap,
+                    (void *)L->d_hdr, (void *)L->d_slot_gen, (void *)L->d_slot_ready, (void *)L->d_bar})
+        cudaFree(p);
+    if (L->h_done) cudaFreeHost(L->h_done);
+    if (L->h_status) cudaFreeHost(L->h_status);
+    if (L->h_flag_ring) cudaFreeHost(L->h_flag_ring);
     for (auto e : L->ev_group) cudaEventDestroy(e);
     for (auto e : L->ev_copy) cudaEventDestroy(e);
-    if (L->ev_pager) cudaEventDestroy(L->ev_pager);
-    if (L->ev_copies) cudaEventDestroy(L->ev_copies);
+    for (cudaEvent_t e : {L->ev_pager, L->ev_copies, L->ev_last})
+        if (e) cudaEventDestroy(e);
     if (L->copy_stream) cudaStreamDestroy(L->copy_stream);
     delete L;
     return WISP_OK;
@@ -375,8 +726,12 @@ int wisp_moe_forward(wisp_layer *L, const void *x, const float *topk_weights,
         return fail(WISP_ERR_INVALID, "wisp_moe_forward: x and out must be 16-byte aligned");
     std::lock_guard<std::mutex> lk(L->mu);
     DeviceGuard guard(L->dev);
+    int rc = take_errors(L);
+    if (rc) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    int rc = run_pager(L, topk_ids, ids_int64, num_tokens, top_k, 0, 1, s);
+    if (L->async && top_k <= L->cap)
+        return forward_async(L, x, topk_weights, topk_ids, ids_int64, num_tokens, top_k, out, s);
+    rc = run_pager(L, topk_ids, ids_int64, num_tokens, top_k, 0, 1, s);
     if (rc) return rc;
     return page_and_compute(L, x, topk_weights, num_tokens, top_k, out, s, true);
 }
@@ -389,8 +744,10 @@ int wisp_ensure_resident(wisp_layer *L, const void *ids, int32_t ids_int64, int3
         return fail(WISP_ERR_INVALID, "wisp_ensure_resident: layer is not in paged mode");
     std::lock_guard<std::mutex> lk(L->mu);
     DeviceGuard guard(L->dev);
+    int rc = take_errors(L);
+    if (rc) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    int rc = run_pager(L, ids, ids_int64, 1, n, 1, 0, s);
+    rc = run_pager(L, ids, ids_int64, 1, n, 1, 0, s);
     if (rc) return rc;
     rc = page_and_compute(L, nullptr, nullptr, 1, n, nullptr, s, false);
     if (rc) return rc;
@@ -406,8 +763,10 @@ int wisp_pager_step(wisp_layer *L, const void *topk_ids, int32_t ids_int64, int3
         return fail(WISP_ERR_INVALID, "wisp_pager_step: bad ids");
     std::lock_guard<std::mutex> lk(L->mu);
     DeviceGuard guard(L->dev);
+    int rc = take_errors(L);
+    if (rc) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    int rc = run_pager(L, topk_ids, ids_int64, num_tokens, top_k, 0, 1, s);
+    rc = run_pager(L, topk_ids, ids_int64, num_tokens, top_k, 0, 1, s);
     if (rc) return rc;
     rc = page_and_compute(L, nullptr, nullptr, num_tokens, top_k, nullptr, s, false);
     if (rc) return rc;
@@ -424,16 +783,21 @@ int wisp_prime_identity(wisp_layer *L, void *stream) {
     if (L->cap != L->E) return fail(WISP_ERR_INVALID, "prime_identity requires cap == num_experts");
     std::lock_guard<std::mutex> lk(L->mu);
     DeviceGuard guard(L->dev);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    WISP_CUDA_TRY(cudaStreamWaitEvent(L->copy_stream, L->ev_copies, 0));
+    int rc = drain(L);
+    if (rc) return rc;
+    std::vector<int32_t> ident(L->E);
+    for (int i = 0; i < L->E; ++i) ident[i] = i;
+    // the copy stream carries copies and flag writes only (no kernels)
     WISP_CUDA_TRY(cudaMemcpyAsync(L->d13, L->h13, (size_t)L->E * L->b13, cudaMemcpyHostToDevice,
                                   L->copy_stream));
     WISP_CUDA_TRY(cudaMemcpyAsync(L->d2, L->h2, (size_t)L->E * L->b2, cudaMemcpyHostToDevice,
                                   L->copy_stream));
-    fill_identity_kernel<<<(L->E + 255) / 256, 256, 0, L->copy_stream>>>(L->d_s2e, L->d_emap, L->E);
-    WISP_CUDA_TRY(cudaGetLastError());
+    WISP_CUDA_TRY(cudaMemcpy(L->d_s2e, ident.data(), sizeof(int32_t) * L->E, cudaMemcpyHostToDevice));
+    WISP_CUDA_TRY(cudaMemcpy(L->d_emap, ident.data(), sizeof(int32_t) * L->E, cudaMemcpyHostToDevice));
+    WISP_CUDA_TRY(cudaMemcpy(L->d_slot_ready, L->d_slot_gen, sizeof(uint32_t) * L->cap,
+                             cudaMemcpyDeviceToDevice));
     WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
-    WISP_CUDA_TRY(cudaStreamWaitEvent(s, L->ev_copies, 0));
+    WISP_CUDA_TRY(cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(stream), L->ev_copies, 0));
     return WISP_OK;
 }
 
@@ -442,46 +806,53 @@ int wisp_resize_cap(wisp_layer *L, int32_t new_cap, void *stream) {
     (void)stream;
     std::lock_guard<std::mutex> lk(L->mu);
     DeviceGuard guard(L->dev);
+    if (L->mode != WISP_MODE_PAGED) return fail(WISP_ERR_INVALID, "wisp_resize_cap: not a paged layer");
     new_cap = std::max(2, std::min((int)new_cap, L->E));
     if (new_cap == L->cap) return WISP_OK;
+    int rc = drain(L);
+    if (rc) return rc;
     WISP_CUDA_TRY(cudaDeviceSynchronize());  // drained barrier, as the reference requires
     const int old = L->cap, keep = std::min(old, new_cap);
     std::vector<int32_t> s2e(old), emap(L->E);
     std::vector<int64_t> tick(old);
+    std::vector<uint32_t> gen(old);
     WISP_CUDA_TRY(cudaMemcpy(s2e.data(), L->d_s2e, sizeof(int32_t) * old, cudaMemcpyDeviceToHost));
     WISP_CUDA_TRY(cudaMemcpy(tick.data(), L->d_tick, sizeof(int64_t) * old, cudaMemcpyDeviceToHost));
     WISP_CUDA_TRY(cudaMemcpy(emap.data(), L->d_emap, sizeof(int32_t) * L->E, cudaMemcpyDeviceToHost));
+    WISP_CUDA_TRY(cudaMemcpy(gen.data(), L->d_slot_gen, sizeof(uint32_t) * old, cudaMemcpyDeviceToHost));
     char *o13 = L->d13, *o2 = L->d2;
     int32_t *os2e = L->d_s2e;
     int64_t *otick = L->d_tick;
+    uint32_t *ogen = L->d_slot_gen, *oready = L->d_slot_ready;
     L->d13 = L->d2 = nullptr;
-    int rc = alloc_state(L, new_cap);
-    if (rc) {
-        cudaFree(L->d13);
-        cudaFree(L->d2);
-        cudaFree(L->d_s2e);
-        cudaFree(L->d_tick);
+    if (alloc_slots(L, new_cap)) {
+        for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->d_s2e, (void *)L->d_tick,
+                        (void *)L->d_slot_gen, (void *)L->d_slot_ready})
+            cudaFree(p);
         L->d13 = o13;
         L->d2 = o2;
         L->d_s2e = os2e;
         L->d_tick = otick;
-        return WISP_ERR_NOMEM;
+        L->d_slot_gen = ogen;
+        L->d_slot_ready = oready;
+        return fail(WISP_ERR_NOMEM, "wisp_resize_cap: HBM allocation failed");
     }
     WISP_CUDA_TRY(cudaMemcpy(L->d13, o13, (size_t)keep * L->b13, cudaMemcpyDeviceToDevice));
     WISP_CUDA_TRY(cudaMemcpy(L->d2, o2, (size_t)keep * L->b2, cudaMemcpyDeviceToDevice));
-    if (new_cap < old) {
+    if (new_cap < old)
         for (int s = new_cap; s < old; ++s)
             if (s2e[s] >= 0) emap[s2e[s]] = -1;
-    }
     s2e.resize(new_cap, -1);
     tick.resize(new_cap, 0);
+    gen.resize(new_cap, 0);
     WISP_CUDA_TRY(cudaMemcpy(L->d_s2e, s2e.data(), sizeof(int32_t) * new_cap, cudaMemcpyHostToDevice));
     WISP_CUDA_TRY(cudaMemcpy(L->d_tick, tick.data(), sizeof(int64_t) * new_cap, cudaMemcpyHostToDevice));
     WISP_CUDA_TRY(cudaMemcpy(L->d_emap, emap.data(), sizeof(int32_t) * L->E, cudaMemcpyHostToDevice));
-    cudaFree(o13);
-    cudaFree(o2);
-    cudaFree(os2e);
-    cudaFree(otick);
+    // every copy has landed at this barrier: generation flags equal the generations
+    WISP_CUDA_TRY(cudaMemcpy(L->d_slot_gen, gen.data(), sizeof(uint32_t) * new_cap, cudaMemcpyHostToDevice));
+    WISP_CUDA_TRY(cudaMemcpy(L->d_slot_ready, gen.data(), sizeof(uint32_t) * new_cap, cudaMemcpyHostToDevice));
+    for (void *p : {(void *)o13, (void *)o2, (void *)os2e, (void *)otick, (void *)ogen, (void *)oready})
+        cudaFree(p);
     L->cap = new_cap;
     return WISP_OK;
 }
@@ -524,10 +895,49 @@ int wisp_layer_buffers(wisp_layer *L, void **scratch_w13, void **scratch_w2, voi
     return WISP_OK;
 }
 
-int wisp_last_forward_info(wisp_layer *L, int64_t *info4) {
-    if (!L || !info4) return fail(WISP_ERR_INVALID, "wisp_last_forward_info: NULL argument");
-    for (int i = 0; i < 4; ++i) info4[i] = L->info[i];
+int wisp_get_telemetry(wisp_layer *L, int64_t *out4) {
+    if (!L || !out4) return fail(WISP_ERR_INVALID, "wisp_get_telemetry: NULL argument");
+    std::lock_guard<std::mutex> lk(L->mu);
+    DeviceGuard guard(L->dev);
+    WISP_CUDA_TRY(cudaDeviceSynchronize());
+    int64_t hdr[7];
+    WISP_CUDA_TRY(cudaMemcpy(hdr, L->d_hdr, sizeof(hdr), cudaMemcpyDeviceToHost));
+    out4[0] = hdr[5];
+    out4[1] = hdr[2];
+    out4[2] = hdr[2] * (L->b13 + L->b2);
+    out4[3] = hdr[6];
     return WISP_OK;
+}
+
+int wisp_layer_sync(wisp_layer *L) {
+    if (!L) return fail(WISP_ERR_INVALID, "wisp_layer_sync: NULL layer");
+    std::lock_guard<std::mutex> lk(L->mu);
+    DeviceGuard guard(L->dev);
+    int rc = drain(L);
+    if (rc) return rc;
+    return take_errors(L);
+}
+
+int wisp_layer_config(wisp_layer *L, int32_t key, int64_t value) {
+    if (!L) return fail(WISP_ERR_INVALID, "wisp_layer_config: NULL layer");
+    std::lock_guard<std::mutex> lk(L->mu);
+    switch (key) {
+        case WISP_CFG_ASYNC:
+            L->async = value != 0;
+            return WISP_OK;
+        case WISP_CFG_WAIT_NS:
+            if (value < 1000000) return fail(WISP_ERR_INVALID, "wisp_layer_config: wait limit below 1 ms");
+            L->wait_ns = value;
+            return WISP_OK;
+        case WISP_CFG_DROP_PAGEINS:
+            L->drop_pageins.store((int)std::max<int64_t>(value, 0));
+            return WISP_OK;
+        case WISP_CFG_TRACE_BUFFER:
+            L->trace = reinterpret_cast<unsigned long long *>(value);
+            return WISP_OK;
+        default:
+            return fail(WISP_ERR_INVALID, "wisp_layer_config: unknown key");
+    }
 }
 
 }  // extern "C"

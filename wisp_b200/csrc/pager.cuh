@@ -1,4 +1,4 @@
-// Device pager (K1) interface shared by the runtime.
+// Device pager (K1) interface shared by the runtime and the forward kernels.
 #pragma once
 #include <stddef.h>
 #include <stdint.h>
@@ -7,39 +7,54 @@
 
 namespace wisp {
 
-// Mailbox (mapped pinned host memory, int32 words) written by the pager:
+// Mailbox (mapped pinned host memory, int32 words) written by the pager; the
+// host hands each forward a mailbox slot that no unfinished page-in task still
+// reads, so the pager never overwrites a mailbox under the reader:
 //   [0] status  [1] groups G  [2] misses  [3] failing group  [4] sum of unique experts
+//   [5] forward-kernel status (slot 0 only)  [6] reserved  [7] sequence number (written last)
 //   [kMbHeader ...]            group first tokens, G+1 entries (last = T)
 //   [kMbHeader + T + 1 ...]    unique experts per group, G entries
-//   [mailbox_miss_offset(T)..] page-in records {expert, slot, group, wait_group}
+//   [mailbox_miss_offset(T)..] page-in records of kMbRec words:
+//                              {expert, slot, group, wait_group, generation, 0, 0, 0}
 constexpr int kMbHeader = 8;
+constexpr int kMbRec = 8;
 inline __host__ __device__ long mailbox_miss_offset(int T) {
-    return ((kMbHeader + 2L * T + 1 + 3) / 4) * 4;
+    return ((kMbHeader + 2L * T + 1 + 7) / 8) * 8;
 }
 inline __host__ __device__ long mailbox_words(int T, int K) {
-    return mailbox_miss_offset(T) + 4L * T * K;
+    return mailbox_miss_offset(T) + (long)kMbRec * T * K;
 }
+
+// Device header words written by the pager (read by the forward kernel).
+enum { kHdrStatus = 0, kHdrGroups = 1, kHdrMisses = 2, kHdrUnique = 3, kHdrWords = 8 };
 
 struct PagerParams {
     const void *ids;
     int ids64, T, K, E, cap, mode, count_forward, single_group;
+    uint32_t seq;  // forward sequence number published in the mailbox
     // state (device)
     int32_t *s2e;
     int64_t *tick;
     int32_t *emap;
-    int64_t *hdr;  // [0] clock, [1..4] forward, miss, hits, evict
+    int64_t *hdr;        // [0] clock, [1..4] forward, miss, hits, evict; [5] groups, [6] unique experts (telemetry)
+    uint32_t *slot_gen;  // [cap] page-in generation of each slot
     // outputs (device)
     int32_t *slots;      // [T*K]
     int32_t *grp_start;  // [T+1]
     int32_t *grp_nu;     // [T]
-    int32_t *u_slot;     // [T*K]       per group at pair offset p0
+    int32_t *grp_nhit;   // [T]         experts resident before the group (first in its unique list)
+    int32_t *u_slot;     // [T*K]       per group at pair offset p0: hits (ascending id), then misses in page-in order
+    int32_t *u_gen;      // [T*K]       slot generation each unique expert waits for (0: none)
     int32_t *u_off;      // [T*K + T]   per group at p0 + g (n_u + 1 entries, relative to p0)
     int32_t *u_pairs;    // [T*K]       pair ids grouped by unique expert
+    int32_t *dev_hdr;    // [kHdrWords]
     // mailbox (device alias of mapped host memory)
     int32_t *mb;
 };
 
-size_t pager_smem_bytes(int E, int cap);
+size_t pager_smem_bytes(int E, int cap, int T, int K);
 int launch_pager(const PagerParams &p, cudaStream_t stream);
+// The pager is run by one whole CTA of kPagerThreads threads (pager_body.cuh).
+constexpr int kPagerThreads = 256;
 
 }  // namespace wisp

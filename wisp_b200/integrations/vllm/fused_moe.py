@@ -284,13 +284,27 @@ class WispMoEState:
             "wisp_moe_forward")
         return out
 
-    def last_forward_info(self) -> dict:
-        """Host-side counters of the last forward: groups, misses, page-in bytes,
-        unique experts summed over groups."""
+    def synchronize(self) -> None:
+        """Wait for this layer's queued forwards (kernels and page-ins) and raise
+        the first error any of them hit (forwards return before their work runs)."""
+        _lib.check(_lib.lib().wisp_layer_sync(self._h), "forward")
+
+    def telemetry(self) -> dict:
+        """Cumulative counters (synchronises): token groups run, misses, page-in
+        bytes, unique experts read summed over groups."""
         info = (ctypes.c_int64 * 4)()
-        _lib.check(_lib.lib().wisp_last_forward_info(self._h, info))
+        _lib.check(_lib.lib().wisp_get_telemetry(self._h, info))
         return {"groups": info[0], "misses": info[1], "pagein_bytes": info[2],
                 "unique_experts": info[3]}
+
+    def configure(self, *, asynchronous: bool | None = None, wait_ns: int | None = None,
+                  drop_pageins: int | None = None) -> None:
+        """Runtime knobs of the native layer (see ``wisp_layer_config``)."""
+        L = _lib.lib()
+        for key, val in ((_lib.CFG_ASYNC, asynchronous), (_lib.CFG_WAIT_NS, wait_ns),
+                         (_lib.CFG_DROP_PAGEINS, drop_pageins)):
+            if val is not None:
+                _lib.check(L.wisp_layer_config(self._h, key, int(val)), "configure")
 
 
 # ---------------------------------------------------------------------------
@@ -332,7 +346,8 @@ def snapshot_expert_stats(reset: bool = True) -> dict:
     for s in _LAYER_STATES:
         f, m, h, _e = s.stats()
         miss, hit, fwd = miss + m, hit + h, fwd + f
-    ws = max((s.last_forward_info()["unique_experts"] for s in _LAYER_STATES), default=0)
+    tel = [s.telemetry() for s in _LAYER_STATES]
+    ws = max((t["unique_experts"] // max(t["groups"], 1) for t in tel), default=0)
     if reset:
         for s in _LAYER_STATES:
             s.stats_miss = 0
