@@ -110,164 +110,194 @@ struct Meta {
     int pair[kMetaP], tok[kMetaP];
 };
 
-// ---- pipelined gate-up (decode sizes) ----------------------------------------
-__device__ __forceinline__ void gu_load(const GroupCompute &a, int slot, int j, int lane,
-                                        uint4 (&wg)[kGuChunks], uint4 (&wu)[kGuChunks]) {
-    const int H = a.H, I = a.I;
-    const __nv_bfloat16 *grow = a.w13 + (size_t)slot * (size_t)(2 * I) * H + (size_t)j * H;
-    const __nv_bfloat16 *urow = grow + (size_t)I * H;
-#pragma unroll
-    for (int m = 0; m < kGuChunks; ++m) {
-        const int c = m * 256 + lane * 8;
-        if (c < H) {
-            wg[m] = ld_cg16(grow + c);
-            wu[m] = ld_cg16(urow + c);
-        }
-    }
+// ---- TMA-fed units (decode sizes) --------------------------------------------
+// Each warp owns kStages shared-memory buffers of kStageBytes with one
+// mbarrier each.  Lane 0 streams a unit's weight rows (contiguous blocks) in
+// with cp.async.bulk; the warp computes from shared memory while the copies of
+// its next units are in flight.  Every mbarrier wait is bounded in time.
+constexpr int kStages = 2;
+constexpr int kStageBytes = 8192;  // >= 2 rows x H (gate-up) and 4 rows x I (down), bf16
+constexpr int kPubLane = 31;       // lane that stores and publishes gate-up rows
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
 }
 
-template <int MAXP>
-__device__ __forceinline__ void gu_compute(const GroupCompute &a, const Meta &m, int u, int j,
-                                           int lane, const uint4 (&wg)[kGuChunks],
-                                           const uint4 (&wu)[kGuChunks]) {
-    const int H = a.H, I = a.I;
-    const int q0 = m.off[u], q1 = m.off[u + 1];
-    for (int qb = q0; qb < q1; qb += MAXP) {  // more pairs than MAXP: further passes, same registers
-        const int np = min(MAXP, q1 - qb);
-        float ag[MAXP], au[MAXP];
-#pragma unroll
-        for (int i = 0; i < MAXP; ++i) {
-            ag[i] = 0.f;
-            au[i] = 0.f;
-        }
-#pragma unroll
-        for (int c8 = 0; c8 < kGuChunks; ++c8) {
-            const int c = c8 * 256 + lane * 8;
-            if (c < H) {
-#pragma unroll
-                for (int i = 0; i < MAXP; ++i) {
-                    if (i < np) {
-                        const uint4 xv = ld_cached16(a.x + (size_t)m.tok[qb + i] * H + c);
-                        ag[i] = dot8(wg[c8], xv, ag[i]);
-                        au[i] = dot8(wu[c8], xv, au[i]);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < MAXP; ++i) {
-            if (i < np) {
-                const float g = round_bf16(warp_sum(ag[i]));
-                const float v = round_bf16(warp_sum(au[i]));
-                if (lane == i) {
-                    const float s = g / (1.0f + expf(-g));
-                    a.act[(size_t)m.pair[qb + i] * I + j] = __float2bfloat16_rn(s * v);
-                }
+// Per-warp copy pipeline state.
+struct WarpPipe {
+    unsigned char *buf;  // kStages * kStageBytes
+    uint64_t *bar;       // kStages mbarriers
+    uint32_t phase;      // bit s: parity to wait for on stage s
+    uint32_t pending;    // bit s: a copy into stage s has not been waited for
+};
+
+// Wait for stage s (bounded); on timeout record it and abort.
+__device__ bool pipe_wait(WarpPipe &w, int s, const ForwardParams &fp) {
+    const uint32_t par = (w.phase >> s) & 1u;
+    if (!mbar_try_wait(w.bar + s, par)) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(w.bar + s, par)) {
+            if ((long long)(globaltimer_ns() - t0) > fp.wait_ns) {
+                set_status(fp.bar, WISP_ERR_TIMEOUT);
+                atomicExch(fp.bar + kBarAbort, 1u);
+                return false;
             }
         }
     }
+    w.phase ^= 1u << s;
+    w.pending &= ~(1u << s);
+    return true;
 }
 
-// Units k = (u - u_lo) * I + j for u in [u_lo, m.nu); this warp takes
-// k = wid, wid + nw, ...; returns false if the kernel is aborting.
+// Before leaving on an abort: let the copies still landing in this warp's
+// buffers finish (each wait bounded), so no copy outlives the block.
+__device__ void pipe_drain(WarpPipe &w, const ForwardParams &fp) {
+    for (int s = 0; s < kStages; ++s) {
+        if (!((w.pending >> s) & 1u)) continue;
+        const uint32_t par = (w.phase >> s) & 1u;
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(w.bar + s, par))
+            if ((long long)(globaltimer_ns() - t0) > fp.wait_ns) break;
+        w.phase ^= 1u << s;
+    }
+    w.pending = 0;
+}
+
+// Lane 0 (the caller has established the slot is ready): copy `n` blocks.
+__device__ __forceinline__ void pipe_issue(WarpPipe &w, int s, const void *src0, uint32_t b0,
+                                           const void *src1, uint32_t b1) {
+    unsigned char *dst = w.buf + s * kStageBytes;
+    fence_proxy_async();
+    mbar_expect_tx(w.bar + s, b0 + b1);
+    bulk_g2s(dst, src0, b0, w.bar + s);
+    if (b1) bulk_g2s(dst + b0, src1, b1, w.bar + s);
+}
+
+// Gate-up units k = (u - u_lo) * I + j, u in [u_lo, m.nu); this warp takes
+// k = wid, wid + nw, ...  Returns false when the kernel is aborting.
 template <int MAXP>
 __device__ bool gateup_units(const GroupCompute &a, const Meta &m, int u_lo, int wid, int nw, int lane,
-                             const ForwardParams &fp) {
-    const int I = a.I;
+                             const ForwardParams &fp, WarpPipe &w, unsigned int *done1) {
+    const int H = a.H, I = a.I;
+    const uint32_t rowb = (uint32_t)H * 2;
     const long total = (long)(m.nu - u_lo) * I;
-    auto ready = [&](int u) -> bool {
-        if (m.gen[u] == 0) return true;
-        int ok = 1;
-        if (lane == 0) ok = wait_slot(fp.slot_ready, m.slot[u], (uint32_t)m.gen[u], fp.bar, fp.wait_ns);
-        return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    auto issue = [&](long k, int s) -> bool {
+        const int u = u_lo + (int)(k / I), j = (int)(k % I);
+        if (m.gen[u] != 0) {  // expert paged in during this call: its slot must have landed
+            int ok = 1;
+            if (lane == 0) ok = wait_slot(fp.slot_ready, m.slot[u], (uint32_t)m.gen[u], fp.bar, fp.wait_ns);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+        }
+        if (lane == 0) {
+            const __nv_bfloat16 *g = a.w13 + (size_t)m.slot[u] * (size_t)(2 * I) * H + (size_t)j * H;
+            pipe_issue(w, s, g, rowb, g + (size_t)I * H, rowb);
+        }
+        w.pending |= 1u << s;
+        return true;
     };
-    uint4 wgA[kGuChunks], wuA[kGuChunks], wgB[kGuChunks], wuB[kGuChunks];
-    long k = wid;
-    if (k >= total) return true;
-    int uA = u_lo + (int)(k / I), jA = (int)(k % I);
-    if (!ready(uA)) return false;
-    gu_load(a, m.slot[uA], jA, lane, wgA, wuA);
-    while (true) {
-        long kn = k + nw;
-        int uB = 0, jB = 0;
-        if (kn < total) {
-            uB = u_lo + (int)(kn / I);
-            jB = (int)(kn % I);
-            if (!ready(uB)) return false;
-            gu_load(a, m.slot[uB], jB, lane, wgB, wuB);
-        }
-        gu_compute<MAXP>(a, m, uA, jA, lane, wgA, wuA);
-        if (kn >= total) return true;
-        k = kn;
-        kn = k + nw;
-        if (kn < total) {
-            uA = u_lo + (int)(kn / I);
-            jA = (int)(kn % I);
-            if (!ready(uA)) return false;
-            gu_load(a, m.slot[uA], jA, lane, wgA, wuA);
-        }
-        gu_compute<MAXP>(a, m, uB, jB, lane, wgB, wuB);
-        if (kn >= total) return true;
-        k = kn;
+    bool ok = true;
+    for (int s = 0; s < kStages && ok; ++s) {
+        const long k = wid + (long)s * nw;
+        if (k < total) ok = issue(k, s);
     }
-}
-
-// ---- pipelined down x weight (decode sizes) --------------------------------------
-__device__ __forceinline__ void dq_load(const GroupCompute &a, int slot, int h0, int lane,
-                                        uint4 (&wv)[4][kDqChunks]) {
-    const int H = a.H, I = a.I;
-    const int nr = min(4, H - h0);
-    const __nv_bfloat16 *wbase = a.w2 + (size_t)slot * (size_t)H * I + (size_t)h0 * I;
-#pragma unroll
-    for (int c4 = 0; c4 < kDqChunks; ++c4) {
-        const int c = c4 * 256 + lane * 8;
-        if (c < I) {
-#pragma unroll
-            for (int r = 0; r < 4; ++r) wv[r][c4] = ld_cg16(wbase + (size_t)(r < nr ? r : 0) * I + c);
+    // publication of the previous unit's rows, one unit late: by then its stores
+    // have completed and the fence costs little
+    // (the stores and the fence are on kPubLane, not on lane 0 which issues the
+    // copies: a fence must not wait for this warp's copies in flight)
+    int pub_u = -1;
+    unsigned pub_n = 0;
+    auto publish = [&]() {
+        if (done1 && pub_n && lane == kPubLane) {
+            __threadfence();
+            atomicAdd(done1 + pub_u, pub_n);
         }
-    }
-}
-
-template <int MAXQ>
-__device__ __forceinline__ void dq_compute(const GroupCompute &a, const Meta &m, int u, int h0,
-                                           int lane, const uint4 (&wv)[4][kDqChunks]) {
-    const int H = a.H, I = a.I;
-    const int nr = min(4, H - h0);
-    const int q0 = m.off[u], q1 = m.off[u + 1];
-    for (int qb = q0; qb < q1; qb += MAXQ) {
-        const int np = min(MAXQ, q1 - qb);
-        float acc[4][MAXQ];
+        pub_n = 0;
+    };
+    long i = 0;
+    for (long k = wid; ok && k < total; k += nw, ++i) {
+        const int s = (int)(i % kStages);
+        if (!pipe_wait(w, s, fp)) {
+            ok = false;
+            break;
+        }
+        publish();
+        const int u = u_lo + (int)(k / I), j = (int)(k % I);
+        const uint4 *gs = reinterpret_cast<const uint4 *>(w.buf + s * kStageBytes);
+        const uint4 *us = reinterpret_cast<const uint4 *>(w.buf + s * kStageBytes + rowb);
+        const int q0 = m.off[u], q1 = m.off[u + 1];
+        for (int qb = q0; qb < q1; qb += MAXP) {
+            const int np = min(MAXP, q1 - qb);
+            float ag[MAXP], au[MAXP];
 #pragma unroll
-        for (int i = 0; i < MAXQ; ++i)
+            for (int t = 0; t < MAXP; ++t) {
+                ag[t] = 0.f;
+                au[t] = 0.f;
+            }
 #pragma unroll
-            for (int r = 0; r < 4; ++r) acc[r][i] = 0.f;
+            for (int c8 = 0; c8 < kGuChunks; ++c8) {
+                const int c = c8 * 256 + lane * 8;
+                if (c < H) {
+                    const uint4 wg = gs[c >> 3], wu = us[c >> 3];
 #pragma unroll
-        for (int c4 = 0; c4 < kDqChunks; ++c4) {
-            const int c = c4 * 256 + lane * 8;
-            if (c < I) {
+                    for (int t = 0; t < MAXP; ++t) {
+                        if (t < np) {
+                            const uint4 xv = ld_cached16(a.x + (size_t)m.tok[qb + t] * H + c);
+                            ag[t] = dot8(wg, xv, ag[t]);
+                            au[t] = dot8(wu, xv, au[t]);
+                        }
+                    }
+                }
+            }
 #pragma unroll
-                for (int i = 0; i < MAXQ; ++i) {
-                    if (i < np) {
-                        const uint4 av = ld_cg16(a.act + (size_t)m.pair[qb + i] * I + c);
-#pragma unroll
-                        for (int r = 0; r < 4; ++r) acc[r][i] = dot8(wv[r][c4], av, acc[r][i]);
+            for (int t = 0; t < MAXP; ++t) {
+                if (t < np) {
+                    const float g = round_bf16(warp_sum(ag[t]));
+                    const float v = round_bf16(warp_sum(au[t]));
+                    if (lane == kPubLane) {  // one lane stores every pair's row j and publishes them
+                        const float sg = g / (1.0f + expf(-g));
+                        a.act[(size_t)m.pair[qb + t] * I + j] = __float2bfloat16_rn(sg * v);
                     }
                 }
             }
         }
-#pragma unroll
-        for (int i = 0; i < MAXQ; ++i) {
-            if (i < np) {
-                const int p = m.pair[qb + i];
-                const float wp = a.topk_w[p];
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const float s = warp_sum(acc[r][i]);
-                    if (lane == 0 && r < nr) a.y[(size_t)p * H + h0 + r] = __float2bfloat16_rn(s * wp);
-                }
-            }
-        }
+        pub_u = u;
+        pub_n = (unsigned)(q1 - q0);
+        __syncwarp();
+        const long kn = k + (long)kStages * nw;
+        if (kn < total) ok = issue(kn, s);
     }
+    if (!ok) {
+        pipe_drain(w, fp);
+        return false;
+    }
+    publish();
+    return true;
 }
 
 // The last of the nu units of row quad q to finish sums the group's tokens.
@@ -283,17 +313,172 @@ __device__ __forceinline__ void quad_arrive(const GroupCompute &a, int q, int nu
     }
 }
 
-template <int MAXQ>
-__device__ void down_units(const GroupCompute &a, const Meta &m, int wid, int nw, int lane) {
-    const int nq = (a.H + 3) / 4;
-    const long total = (long)m.nu * nq;
-    uint4 A[4][kDqChunks];
-    for (long k = wid; k < total; k += nw) {
-        const int u = (int)(k / nq), q = (int)(k % nq);
-        dq_load(a, m.slot[u], q * 4, lane, A);
-        dq_compute<MAXQ>(a, m, u, q * 4, lane, A);
-        quad_arrive(a, q, m.nu, lane);
+// Wait (lane 0, bounded) until every gate-up row of expert u is published.
+__device__ bool wait_act(const unsigned int *done1, int u, unsigned int need, const ForwardParams &fp,
+                         int lane) {
+    int ok = 1;
+    if (lane == 0) {
+        volatile const unsigned int *f = done1 + u;
+        if (*f < need) {
+            volatile unsigned int *vabort = fp.bar + kBarAbort;
+            const unsigned long long t0 = globaltimer_ns();
+            while (*f < need) {
+                if (*vabort) {
+                    ok = 0;
+                    break;
+                }
+                if ((long long)(globaltimer_ns() - t0) > fp.wait_ns) {
+                    set_status(fp.bar, WISP_ERR_TIMEOUT);
+                    atomicExch(fp.bar + kBarAbort, 1u);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __threadfence();
     }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Down units k = u * nq + q (four rows h0 = 4q.. of expert u, one contiguous
+// block of W2) for u < m.nu.  Units go out in chunks of kDownChunk
+// consecutive units (mostly one expert, whose activation rows then stay in
+// registers), chunks round-robin over the warps.  With `done1`, a unit first
+// waits until its expert's activations are complete (its W2 copy is already
+// in flight).  The weighted y of every unit goes to global memory; at the end
+// the warp fences once and its lanes arrive on the row quads' counters in
+// parallel; the last arrival of a quad sums the group's tokens over k in
+// routing order for those rows.
+constexpr int kDownChunk = 4;
+template <int MAXQ>
+__device__ bool down_units(const GroupCompute &a, const Meta &m, int wid, int nw, int lane,
+                           const ForwardParams &fp, WarpPipe &w, const unsigned int *done1) {
+    const int H = a.H, I = a.I;
+    const int nq = (H + 3) / 4;
+    const long total = (long)m.nu * nq;
+    // the i-th unit of this warp (may be >= total past the last one)
+    auto unit_of = [&](long i) -> long {
+        return ((long)wid + (i / kDownChunk) * nw) * kDownChunk + (i % kDownChunk);
+    };
+    long count = 0;
+    while (unit_of(count) < total) ++count;  // at most a few chunks per warp
+    if (count == 0) return true;
+    // a unit of an expert paged in during this call reads its slot only after
+    // the page-in has landed
+    auto issue = [&](long i, int s) -> bool {
+        const long k = unit_of(i);
+        const int u = (int)(k / nq), q = (int)(k % nq);
+        const int nr = min(4, H - 4 * q);
+        if (m.gen[u] != 0) {
+            int rdy = 1;
+            if (lane == 0) rdy = wait_slot(fp.slot_ready, m.slot[u], (uint32_t)m.gen[u], fp.bar, fp.wait_ns);
+            if (!__shfl_sync(0xffffffffu, rdy, 0)) return false;
+        }
+        if (lane == 0)
+            pipe_issue(w, s, a.w2 + (size_t)m.slot[u] * (size_t)H * I + (size_t)(4 * q) * I,
+                       (uint32_t)nr * I * 2, nullptr, 0);
+        w.pending |= 1u << s;
+        return true;
+    };
+    bool ok = true;
+    for (int s = 0; s < kStages && ok; ++s)
+        if (s < count) ok = issue(s, s);
+    uint4 act[MAXQ][kDqChunks];
+    int act_u = -1;
+    for (long i = 0; ok && i < count; ++i) {
+        const int s = (int)(i % kStages);
+        const long k = unit_of(i);
+        const int u = (int)(k / nq), q = (int)(k % nq), h0 = 4 * q;
+        const int q0 = m.off[u], q1 = m.off[u + 1];
+        if (done1 && u != act_u && !wait_act(done1, u, (unsigned)(I * (q1 - q0)), fp, lane)) {
+            ok = false;
+            break;
+        }
+        const bool cached = (q1 - q0) <= MAXQ;
+        if (cached && u != act_u) {  // this expert's activation rows, reused by its next quads
+#pragma unroll
+            for (int t = 0; t < MAXQ; ++t)
+                if (t < q1 - q0)
+#pragma unroll
+                    for (int c4 = 0; c4 < kDqChunks; ++c4) {
+                        const int c = c4 * 256 + lane * 8;
+                        if (c < I) act[t][c4] = ld_cg16(a.act + (size_t)m.pair[q0 + t] * I + c);
+                    }
+        }
+        act_u = u;
+        if (!pipe_wait(w, s, fp)) {
+            ok = false;
+            break;
+        }
+        const int nr = min(4, H - h0);
+        const uint4 *ws = reinterpret_cast<const uint4 *>(w.buf + s * kStageBytes);
+        for (int qb = q0; qb < q1; qb += MAXQ) {
+            const int np = min(MAXQ, q1 - qb);
+            float acc[4][MAXQ];
+#pragma unroll
+            for (int t = 0; t < MAXQ; ++t)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[r][t] = 0.f;
+#pragma unroll
+            for (int c4 = 0; c4 < kDqChunks; ++c4) {
+                const int c = c4 * 256 + lane * 8;
+                if (c < I) {
+                    uint4 wv[4];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) wv[r] = ws[((r < nr ? r : 0) * I + c) >> 3];
+#pragma unroll
+                    for (int t = 0; t < MAXQ; ++t) {
+                        if (t < np) {
+                            const uint4 av =
+                                cached ? act[t][c4] : ld_cg16(a.act + (size_t)m.pair[qb + t] * I + c);
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) acc[r][t] = dot8(wv[r], av, acc[r][t]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < MAXQ; ++t) {
+                if (t < np) {
+                    const int p = m.pair[qb + t];
+                    const float wp = a.topk_w[p];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float sum = warp_sum(acc[r][t]);
+                        if (lane == r && r < nr) a.y[(size_t)p * H + h0 + r] = __float2bfloat16_rn(sum * wp);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (i + kStages < count) ok = issue(i + kStages, s);
+    }
+    if (!ok) {
+        pipe_drain(w, fp);
+        return false;
+    }
+    // arrivals: one fence, then one lane per unit
+    __threadfence();
+    __syncwarp();
+    for (long ib = 0; ib < count; ib += 32) {
+        const long i = ib + lane;
+        int last = 0, q = 0;
+        if (i < count) {
+            q = (int)(unit_of(i) % nq);
+            last = (atomicAdd(&a.counters[q], 1) == m.nu - 1);
+        }
+        unsigned todo = __ballot_sync(0xffffffffu, last);
+        if (todo) __threadfence();
+        while (todo) {
+            const int l = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int ql = __shfl_sync(0xffffffffu, q, l);
+            combine_rows(a, ql * 4, 4, lane, 32);
+            if (lane == 0) a.counters[ql] = 0;
+        }
+    }
+    return true;
 }
 
 // Generic (non-pipelined) bodies for groups beyond the shared-memory lists.
@@ -444,9 +629,41 @@ __device__ bool load_meta(const ForwardParams &fp, int g, long p0, int nu, int n
     return true;
 }
 
+// Bounded wait (thread 0 of the block) until *word reaches `want`; then every
+// thread of the block sees the words written before it.
+__device__ bool block_wait_word(const unsigned int *word, unsigned int want, const ForwardParams &fp,
+                                bool equal) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        volatile const unsigned int *f = word;
+        volatile unsigned int *vabort = fp.bar + kBarAbort;
+        const unsigned long long t0 = globaltimer_ns();
+        while (equal ? (*f != want) : (*f < want)) {
+            if (*vabort) {
+                ok = 0;
+                break;
+            }
+            if ((long long)(globaltimer_ns() - t0) > fp.wait_ns) {
+                set_status(fp.bar, WISP_ERR_TIMEOUT);
+                atomicExch(fp.bar + kBarAbort, 1u);
+                ok = 0;
+                break;
+            }
+            __nanosleep(32);
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
 // FAST: decode sizes (every group's lists fit in shared memory, H <= 2048,
-// I <= 1024): speculative start and pipelined units.  Otherwise the generic
-// bodies.  The host picks the variant from the shapes alone.
+// I <= 1024): TMA-fed warp units, a speculative start, and for a call that
+// forms one token group no grid barrier at all (dataflow counters).
+// Otherwise the generic bodies with grid barriers between phases.  The host
+// picks the variant from the shapes alone.
 template <int MAXP, bool FAST>
 __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(const __grid_constant__ ForwardParams a) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -456,6 +673,7 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
     const int nwarps = gridDim.x * kWarpsPerBlock;
     const int gw = blockIdx.x * kWarpsPerBlock + warp;
     const PagerParams &pg = a.pg;
+    unsigned int *done1 = a.flow + kFlowDone1 + a.epoch * kFlowMaxU;
     unsigned long long *tr = a.trace;
 #define WISP_TRACE(slot)                                                                 \
     do {                                                                                 \
@@ -468,20 +686,59 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
     WISP_TRACE(0);
     WISP_TRACE0(0);
 
-    // ---- phase 0: pager on block 0, speculative gate-up on the others --------------
-    if (blockIdx.x == 0) {
-        pager_body(pg, smem);
-        WISP_TRACE0(1);
-    } else if (FAST && build_spec_meta(a, meta, reinterpret_cast<int *>(smem))) {
-        GroupCompute gc = a.gc;
-        gc.t0 = 0;
-        gc.t1 = pg.T;
-        gateup_units<MAXP>(gc, meta, 0, gw - kWarpsPerBlock, nwarps - kWarpsPerBlock, lane, a);
-        WISP_TRACE(1);
+    // per-warp copy pipelines (FAST variant); buffers overlay the pager's shared
+    // memory, which block 0 is done with before its first copy
+    __shared__ __align__(8) uint64_t s_bars[kWarpsPerBlock][kStages];
+    WarpPipe pipe{};
+    if (FAST) {
+        pipe.buf = smem + (size_t)warp * kStages * kStageBytes;
+        pipe.bar = s_bars[warp];
+        if (lane == 0) {
+            for (int st = 0; st < kStages; ++st) mbar_init(pipe.bar + st, 1);
+            fence_proxy_async();
+        }
+        __syncwarp();
     }
-    if (!grid_barrier(a.bar, a.wait_ns)) goto done;
-    WISP_TRACE0(2);
-    if (blockIdx.x == 0) pager_finish(pg, smem, a.publish != 0);
+
+    // ---- phase 0 ------------------------------------------------------------------
+    // block 0: pager, publish its outputs, wait until no block still reads the
+    // pre-call expert map, write the new state back.  Other blocks: read the
+    // pre-call map (speculation lists), say so, run gate-up for the experts
+    // that were resident before the call.
+    bool spec_here = false;
+    if (blockIdx.x == 0) {
+        if (tid == 0) {  // the counters the next launch uses start at zero
+            a.flow[kFlowSpecRead + (a.epoch ^ 1)] = 0;
+        }
+        for (int i = tid; i < kFlowMaxU; i += kFwdThreads)
+            a.flow[kFlowDone1 + (a.epoch ^ 1) * kFlowMaxU + i] = 0;
+        pager_body(pg, smem);
+        if (tid == 0) {
+            __threadfence();
+            *reinterpret_cast<volatile unsigned int *>(a.flow + kFlowPagerDone) = pg.seq;
+        }
+        WISP_TRACE0(1);
+        if (!block_wait_word(a.flow + kFlowSpecRead + a.epoch, gridDim.x - 1, a, false)) goto done;
+        pager_finish(pg, smem, a.publish != 0);
+        WISP_TRACE0(2);
+    } else {
+        if (FAST) spec_here = build_spec_meta(a, meta, reinterpret_cast<int *>(smem));
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(a.flow + kFlowSpecRead + a.epoch, 1u);
+        }
+        if (spec_here) {
+            GroupCompute gc = a.gc;
+            gc.t0 = 0;
+            gc.t1 = pg.T;
+            gateup_units<MAXP>(gc, meta, 0, gw - kWarpsPerBlock, nwarps - kWarpsPerBlock, lane, a, pipe,
+                               done1);
+        }
+        __syncthreads();
+        WISP_TRACE(1);
+        if (!block_wait_word(a.flow + kFlowPagerDone, pg.seq, a, true)) goto done;
+    }
     {
         const int status = __ldcg(pg.dev_hdr + kHdrStatus);
         if (status != WISP_OK) {
@@ -489,51 +746,71 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
             goto done;
         }
         const int G = __ldcg(pg.dev_hdr + kHdrGroups);
-        const int K = a.gc.K, H = a.gc.H, I = a.gc.I;
+        const int K = a.gc.K;
         const int P = pg.T * pg.K;
         // mirrors build_spec_meta's condition: one group <=> the experts fit the cap
         const bool spec_ran = FAST && (G == 1) && (P <= kSpecMaxPairs) && (gridDim.x > 1) && pg.E <= 1024;
-        for (int g = 0; g < G; ++g) {
+        if (FAST && G == 1) {
+            // ---- one group: dataflow, no grid barrier -------------------------------------
             GroupCompute gc = a.gc;
-            const int t0 = __ldcg(pg.grp_start + g), t1 = __ldcg(pg.grp_start + g + 1);
-            const long p0 = (long)t0 * K;
-            const int nu = __ldcg(pg.grp_nu + g);
-            const int u_lo = (g == 0 && spec_ran) ? __ldcg(pg.grp_nhit + 0) : 0;
-            gc.t0 = t0;
+            const int t1 = __ldcg(pg.grp_start + 1);
+            const int nu = __ldcg(pg.grp_nu + 0);
+            const int u_lo = spec_ran ? __ldcg(pg.grp_nhit + 0) : 0;
+            gc.t0 = 0;
             gc.t1 = t1;
-            if (FAST) load_meta(a, g, p0, nu, (t1 - t0) * K, meta);
-            // phase 1: gate-up + SiLU-mul
-            if (FAST) {
-                gateup_units<MAXP>(gc, meta, u_lo, gw, nwarps, lane, a);
-            } else {
-                gc.u_slot = pg.u_slot + p0;
-                gc.u_off = pg.u_off + p0 + g;
-                gc.u_pairs = pg.u_pairs + p0;
-                gateup_generic<MAXP>(gc, pg.u_gen + p0, u_lo, nu, gw, nwarps, lane, a);
-            }
+            load_meta(a, 0, 0, nu, t1 * K, meta);
+            if (!gateup_units<MAXP>(gc, meta, u_lo, gw, nwarps, lane, a, pipe, done1)) goto done;
             __syncthreads();
             WISP_TRACE(2);
-            if (!grid_barrier(a.bar, a.wait_ns)) goto done;
-            WISP_TRACE0(3);
-            // phase 2: down x weight, last arrival per row quad combines
-            if (FAST) {
-                down_units<MAXQ>(gc, meta, gw, nwarps, lane);
-            } else {
-                gc.u_slot = pg.u_slot + p0;
-                gc.u_off = pg.u_off + p0 + g;
-                gc.u_pairs = pg.u_pairs + p0;
-                down_generic<MAXQ>(gc, nu, gw, nwarps, lane);
-            }
+            down_units<MAXQ>(gc, meta, gw, nwarps, lane, a, pipe, done1);
             __syncthreads();
             WISP_TRACE(3);
-            if (g + 1 < G) {
-                // later groups may page into slots this group read: publish "done"
-                if (!grid_barrier(a.bar, a.wait_ns)) goto done;
-                if (blockIdx.x == 0 && tid == 0) {
-                    *reinterpret_cast<volatile unsigned long long *>(a.done_word) =
-                        ((unsigned long long)pg.seq << 32) | (unsigned)(g + 1);
-                    __threadfence_system();
+        } else {
+            // ---- several groups (or the generic variant): grid barriers between phases ---------
+            if (!grid_barrier(a.bar, a.wait_ns)) goto done;
+            const int H = a.gc.H, I = a.gc.I;
+            for (int g = 0; g < G; ++g) {
+                GroupCompute gc = a.gc;
+                const int t0 = __ldcg(pg.grp_start + g), t1 = __ldcg(pg.grp_start + g + 1);
+                const long p0 = (long)t0 * K;
+                const int nu = __ldcg(pg.grp_nu + g);
+                gc.t0 = t0;
+                gc.t1 = t1;
+                if (FAST) load_meta(a, g, p0, nu, (t1 - t0) * K, meta);
+                // phase 1: gate-up + SiLU-mul
+                if (FAST) {
+                    gateup_units<MAXP>(gc, meta, 0, gw, nwarps, lane, a, pipe, nullptr);
+                } else {
+                    gc.u_slot = pg.u_slot + p0;
+                    gc.u_off = pg.u_off + p0 + g;
+                    gc.u_pairs = pg.u_pairs + p0;
+                    gateup_generic<MAXP>(gc, pg.u_gen + p0, 0, nu, gw, nwarps, lane, a);
                 }
+                __syncthreads();
+                WISP_TRACE(2);
+                if (!grid_barrier(a.bar, a.wait_ns)) goto done;
+                // phase 2: down x weight, last arrival per row quad combines
+                if (FAST) {
+                    down_units<MAXQ>(gc, meta, gw, nwarps, lane, a, pipe, nullptr);
+                } else {
+                    gc.u_slot = pg.u_slot + p0;
+                    gc.u_off = pg.u_off + p0 + g;
+                    gc.u_pairs = pg.u_pairs + p0;
+                    down_generic<MAXQ>(gc, nu, gw, nwarps, lane);
+                }
+                __syncthreads();
+                WISP_TRACE(3);
+                if (g + 1 < G) {
+                    // later groups may page into slots this group read: publish "done"
+                    if (!grid_barrier(a.bar, a.wait_ns)) goto done;
+                    if (blockIdx.x == 0 && tid == 0) {
+                        *reinterpret_cast<volatile unsigned long long *>(a.done_word) =
+                            ((unsigned long long)pg.seq << 32) | (unsigned)(g + 1);
+                        __threadfence_system();
+                    }
+                }
+                (void)H;
+                (void)I;
             }
         }
     }
@@ -582,8 +859,11 @@ int launch_forward(const ForwardParams &p, int max_tokens_per_group, cudaStream_
     size_t smem = pager_smem_bytes(p.pg.E, p.pg.cap, p.pg.T, p.pg.K);
     smem = smem > sizeof(int) * 1024 ? smem : sizeof(int) * 1024;  // speculation's expert index
     const bool fast = (long)p.pg.T * p.pg.K <= kMetaP && p.gc.H <= kGuChunks * 256 &&
-                      p.gc.I <= kDqChunks * 256;
+                      p.gc.I <= kDqChunks * 256 && 2L * 2 * p.gc.H <= kStageBytes &&
+                      4L * 2 * p.gc.I <= kStageBytes;
     if (fast) {
+        const size_t stages = (size_t)kWarpsPerBlock * kStages * kStageBytes;
+        smem = smem > stages ? smem : stages;
         if (max_tokens_per_group <= 1) return launch_t<1, true>(p, smem, stream);
         if (max_tokens_per_group <= 2) return launch_t<2, true>(p, smem, stream);
         if (max_tokens_per_group <= 4) return launch_t<4, true>(p, smem, stream);

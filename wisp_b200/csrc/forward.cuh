@@ -21,9 +21,23 @@ struct ForwardParams {
     long long wait_ns;              // limit of any single wait
     int *status_word;               // mapped host: sticky kernel status, cleared by the host
     int publish;                    // block 0 publishes the page-in list (paged mode)
+    // dataflow words (device, per layer, kFlowWords): see kFlow* below
+    unsigned int *flow;
+    int epoch;                      // launch parity: which set of counters this launch uses
     // optional %globaltimer trace (debug): [0..7] block 0 milestones, then 4 words per block
     unsigned long long *trace;
 };
+
+// Dataflow words: [kFlowPagerDone] sequence number of the call whose pager
+// outputs are complete; [kFlowSpecRead + e] blocks done reading the pre-call
+// expert map; [kFlowDone1 + e * kFlowMaxU + u] gate-up pairs finished for
+// unique expert u.  e is the launch parity; a launch zeroes the other set,
+// which the next launch uses.
+constexpr int kFlowMaxU = 256;
+constexpr int kFlowPagerDone = 0;
+constexpr int kFlowSpecRead = 1;
+constexpr int kFlowDone1 = 8;
+constexpr int kFlowWords = kFlowDone1 + 2 * kFlowMaxU;
 
 int launch_forward(const ForwardParams &p, int max_tokens_per_group, cudaStream_t stream);
 

@@ -100,6 +100,8 @@ struct wisp_layer {
     int64_t *d_tick = nullptr, *d_hdr = nullptr;
     uint32_t *d_slot_gen = nullptr, *d_slot_ready = nullptr;
     unsigned int *d_bar = nullptr;
+    unsigned int *d_flow = nullptr;  // forward-kernel dataflow words (kFlowWords)
+    int kparity = 0;                 // parity of the forward-kernel launches
     // per-call workspace, grown on demand
     int wsT = -1, wsK = 0;
     int32_t *d_slots = nullptr, *d_grp_start = nullptr, *d_grp_nu = nullptr, *d_grp_nhit = nullptr,
@@ -425,6 +427,7 @@ int drain(wisp_layer *L) {
 int reset_cold(wisp_layer *L) {
     WISP_CUDA_TRY(cudaDeviceSynchronize());
     WISP_CUDA_TRY(cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords));
+    WISP_CUDA_TRY(cudaMemset(L->d_flow, 0, sizeof(unsigned int) * kFlowWords));
     WISP_CUDA_TRY(cudaMemset(L->d_s2e, 0xff, sizeof(int32_t) * L->cap));
     WISP_CUDA_TRY(cudaMemset(L->d_emap, 0xff, sizeof(int32_t) * L->E));
     WISP_CUDA_TRY(cudaMemset(L->d_tick, 0, sizeof(int64_t) * L->cap));
@@ -449,6 +452,7 @@ int take_errors(wisp_layer *L) {
         // the pager rejected the ids before touching any state
         if (!rc) {
             cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords);
+            cudaMemset(L->d_flow, 0, sizeof(unsigned int) * kFlowWords);
             cudaDeviceSynchronize();
         }
         return fail(code, "wisp: an earlier forward routed an expert id outside [0, " +
@@ -575,6 +579,8 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
     fp.wait_ns = L->wait_ns;
     fp.status_word = L->d_status;
     fp.trace = L->trace;
+    fp.flow = L->d_flow;
+    fp.epoch = L->kparity;
     const bool paged = L->mode == WISP_MODE_PAGED;
     fp.publish = paged ? 1 : 0;
     int slot = 0;
@@ -598,6 +604,7 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
         if (paged) L->mb_busy[slot].store(0);
         return rc;
     }
+    L->kparity ^= 1;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
     if (paged) engine_for(L->dev)->submit(L, fp.pg.seq, T, slot);
     return WISP_OK;
@@ -663,11 +670,13 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
         return bail(fail(WISP_ERR_NOMEM, "wisp_layer_create: HBM allocation failed"));
     if (cudaMalloc(&L->d_emap, sizeof(int32_t) * num_experts) != cudaSuccess ||
         cudaMalloc(&L->d_hdr, sizeof(int64_t) * 8) != cudaSuccess ||
-        cudaMalloc(&L->d_bar, sizeof(unsigned int) * kBarWords) != cudaSuccess)
+        cudaMalloc(&L->d_bar, sizeof(unsigned int) * kBarWords) != cudaSuccess ||
+        cudaMalloc(&L->d_flow, sizeof(unsigned int) * kFlowWords) != cudaSuccess)
         return bail(fail(WISP_ERR_NOMEM, "wisp_layer_create: device allocation failed"));
     if (cudaMemset(L->d_emap, 0xff, sizeof(int32_t) * num_experts) != cudaSuccess ||
         cudaMemset(L->d_hdr, 0, sizeof(int64_t) * 8) != cudaSuccess ||
         cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords) != cudaSuccess ||
+        cudaMemset(L->d_flow, 0, sizeof(unsigned int) * kFlowWords) != cudaSuccess ||
         cudaHostAlloc(&L->h_done, sizeof(unsigned long long), cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer((void **)&L->d_done, L->h_done, 0) != cudaSuccess ||
         cudaHostAlloc(&L->h_status, sizeof(int32_t), cudaHostAllocMapped) != cudaSuccess ||
@@ -698,7 +707,8 @@ int wisp_layer_destroy(wisp_layer *L) {
     cudaDeviceSynchronize();
     free_ws(L);
     for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->d_s2e, (void *)L->d_tick, (void *)L->d_emap,
-                    (void *)L->d_hdr, (void *)L->d_slot_gen, (void *)L->d_slot_ready, (void *)L->d_bar})
+                    (void *)L->d_hdr, (void *)L->d_slot_gen, (void *)L->d_slot_ready, (void *)L->d_bar,
+                    (void *)L->d_flow})
         cudaFree(p);
     if (L->h_done) cudaFreeHost(L->h_done);
     if (L->h_status) cudaFreeHost(L->h_status);

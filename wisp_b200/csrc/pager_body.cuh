@@ -21,8 +21,8 @@
 // compute needs (slot of every (t, k) pair, per-group unique-slot lists with
 // their pairs, the device header); pager_finish then writes the LRU state
 // back and publishes the page-in list to the host mailbox.  The forward
-// kernel calls pager_finish after its first grid barrier, so that the other
-// blocks can read the pre-call expert map meanwhile.
+// kernel calls pager_finish only once every other block has finished reading
+// the pre-call expert map (for its speculative start).
 #pragma once
 #include "common.cuh"
 #include "pager.cuh"
@@ -479,6 +479,7 @@ finish:
     }
     if (S.grp != a.grp_start)
         for (int g = tid; g <= sc.G; g += kThreads) a.grp_start[g] = S.grp[g];
+    __threadfence();  // every thread's outputs visible device-wide before the CTA moves on
     __syncthreads();
 }
 
