@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--cap", type=int, default=32)
     ap.add_argument("--layers", type=int, default=SHAPE.layers)
     ap.add_argument("--no-resident", action="store_true", help="skip the resident-decode phase")
+    ap.add_argument("--phase", default="all", choices=["all", "resident"],
+                    help="'resident' runs only the resident-decode region (profiling: the paged "
+                         "forward waits on page-ins a host thread issues during the launch, which "
+                         "a kernel-serialising profiler would stall)")
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     return ap.parse_args()
 
@@ -150,6 +154,27 @@ def routing(steps, layers, batch):
     return ids, w
 
 
+def profile_traffic(name: str):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary
+    (a line ``traffic_bytes_per_launch: N``), or None."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def algorithmic_bytes(unique_experts: int, tokens: int, launches: int) -> int:
+    """Bytes a layer forward must move (expert weights read once per group,
+    activations in and out, routing ids and weights)."""
+    return (unique_experts * SHAPE.expert_bytes + tokens * SHAPE.hidden * 2 * 2
+            + tokens * SHAPE.top_k * (4 + 4)) if launches else 0
+
+
 def run_wisp(args):
     from wisp_b200.integrations.vllm.fused_moe import WispMoEState
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -157,6 +182,8 @@ def run_wisp(args):
     hbm_peak, peak_src = peaks()
     L, B, C = args.layers, args.batch, args.cap
     total = args.warmup + args.steps
+    if args.phase == "resident":
+        return resident_only(args, dev, hbm_peak, peak_src)
     t0 = time.time()
     masters = make_masters(L, dev)
     states = [WispMoEState(h13, h2, C, "paged", dev, i) for i, (h13, h2) in enumerate(masters)]
@@ -190,13 +217,20 @@ def run_wisp(args):
     for st in states:
         st.synchronize()
     tel1 = [st.telemetry() for st in states]
-    pagein_bytes = sum(b["pagein_bytes"] - a["pagein_bytes"] for a, b in zip(tel0, tel1))
+
+    def delta(key):
+        return sum(b[key] - a[key] for a, b in zip(tel0, tel1))
+
+    pagein_bytes = delta("pagein_bytes")
+    launches = delta("kernel_launches")
+    unique = delta("unique_experts")
     after = [st.stats() for st in states]
     misses = sum(a[1] - b[1] for a, b in zip(after, before))
     hits = sum(a[2] - b[2] for a, b in zip(after, before))
     tok_s = B * args.steps / (ms * 1e-3)
 
-    # end to end: host routing + hidden states copied in, output copied out, every step
+    # end to end through the public API: routing + hidden states copied in from
+    # pinned host memory and the output copied back, every step
     ids_h = torch.from_numpy(ids_np).pin_memory()
     w_h = torch.from_numpy(w_np).pin_memory()
     x_h = wl.hidden_states(B, SHAPE.hidden, seed=0).pin_memory()
@@ -204,10 +238,7 @@ def run_wisp(args):
     ids_s = torch.empty((L, B, SHAPE.top_k), dtype=ids_d.dtype, device=dev)
     w_s = torch.empty((L, B, SHAPE.top_k), dtype=w_d.dtype, device=dev)
     e2e_steps = min(args.steps, 8)
-    # re-run the same trace window on fresh state is not needed: e2e measures the same
-    # steady-state loop over the next routing steps, wrapping the trace
     torch.cuda.synchronize()
-    e0 = time.perf_counter()
     ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev2.record()
     for j in range(e2e_steps):
@@ -222,19 +253,42 @@ def run_wisp(args):
     torch.cuda.synchronize()
     e2e_ms = ev2.elapsed_time(ev3)
     e2e = {"value": B * e2e_steps / (e2e_ms * 1e-3), "unit": "tok/s",
-           "h2d_bytes_per_step": int(ids_s.numel() * ids_s.element_size() + w_s.numel() * 4
-                                     + x_h.numel() * 2),
-           "d2h_bytes_per_step": int(out_h.numel() * 2), "wall_s": time.perf_counter() - e0}
+           "h2d_bytes_per_step": int(ids_s.numel() * ids_s.element_size()
+                                     + w_s.numel() * w_s.element_size()
+                                     + x_h.numel() * x_h.element_size()),
+           "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()),
+           "steps": e2e_steps}
 
     h2d = h2d_peak_gbs(dev)
     pagein_gbs = pagein_bytes / (ms * 1e-3) / 1e9
-    res = {}
+    # step roofline: the slower of the HBM bytes at the HBM peak and the page-in
+    # bytes at the measured pinned-H2D peak, divided by the measured time
+    hbm_bytes = algorithmic_bytes(unique, B * L * args.steps, launches)
+    hbm_s = hbm_bytes / (hbm_peak * 1e9)
+    link_s = pagein_bytes / (h2d * 1e9)
+    step_roof = {"hbm_bytes": hbm_bytes, "pagein_bytes": pagein_bytes, "hbm_s": hbm_s,
+                 "link_s": link_s, "measured_s": ms * 1e-3,
+                 "bound": "h2d" if link_s >= hbm_s else "hbm",
+                 "frac": max(hbm_s, link_s) / (ms * 1e-3)}
     for st in states:
         st.close()
     del states
     torch.cuda.empty_cache()
+    res = {}
     if not args.no_resident:
-        res = resident_phase(args, masters, dev, hbm_peak)
+        for rb in sorted({B, 1}, reverse=True):
+            res[f"batch{rb}"] = resident_phase(args, masters, dev, hbm_peak, rb)
+    del masters
+
+    roofline = None
+    if res:
+        r = res[f"batch{B}"]
+        roofline = {"bound": "hbm", "kernel": "forward_kernel",
+                    "region": f"resident decode (cap = E), batch {B}, {r['layers']} layers",
+                    "achieved": r["hbm_gbs"], "peak": hbm_peak, "unit": "GB/s",
+                    "frac": r["frac"], "peak_src": peak_src,
+                    "traffic": profile_traffic(f"forward_kernel_resident_decode_b{B}.md"),
+                    "bytes_per_launch": r["bytes_per_launch"], "us_per_launch": r["us_per_launch"]}
 
     line = {
         "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
@@ -244,8 +298,11 @@ def run_wisp(args):
         "config": {"workload": f"qwen3-30b-a3b {L}-layer expert stack, decode batch {B}, cap {C}",
                    "layers": L, "batch": B, "cap": C, "experts": SHAPE.experts,
                    "top_k": SHAPE.top_k, "hidden": SHAPE.hidden, "inter": SHAPE.inter,
-                   "routing": "zipf1.1 reuse0.6", "l2": "inputs larger than L2 (weights stream "
-                   "from HBM each step: >= 8 experts x 9.4 MB per layer)"},
+                   "routing": "zipf1.1 reuse0.6", "l2": "inputs larger than L2 (each step reads "
+                   "every layer's routed experts, >= 48 x 8 x 9.4 MB, from HBM)"},
+        "gpu_launches": launches,
+        "roofline": roofline,
+        "step_roofline": step_roof,
         "pagein": {"gbs": pagein_gbs, "h2d_peak_gbs": h2d, "frac": pagein_gbs / h2d,
                    "misses": misses, "hits": hits, "bytes": pagein_bytes},
         "resident_decode": res,
@@ -256,12 +313,31 @@ def run_wisp(args):
     return line
 
 
-def resident_phase(args, masters, dev, hbm_peak):
-    """Resident-expert decode (cap = E, prime_identity): HBM-bound; reports
-    tok/s and achieved HBM GB/s of the whole layer forward."""
+def resident_only(args, dev, hbm_peak, peak_src):
+    """The resident-decode region alone, at the given batch (profiling runs)."""
+    masters = make_masters(min(args.layers, 24), dev)
+    r = resident_phase(args, masters, dev, hbm_peak, args.batch)
+    return {"metric": "resident decode tok/s (cap = E)", "value": r["tok_s_per_layer_stack"],
+            "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["us_per_layer"] * r["layers"] / 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"qwen3-30b-a3b {r['layers']}-layer expert stack, resident decode "
+                                   f"batch {args.batch}"},
+            "gpu_launches": r["launches"],
+            "roofline": {"bound": "hbm", "kernel": "forward_kernel", "achieved": r["hbm_gbs"],
+                         "peak": hbm_peak, "unit": "GB/s", "frac": r["frac"], "peak_src": peak_src,
+                         "bytes_per_launch": r["bytes_per_launch"], "us_per_launch": r["us_per_launch"]},
+            "resident_decode": r}
+
+
+def resident_phase(args, masters, dev, hbm_peak, batch):
+    """Resident-expert decode (cap = E, prime_identity): one forward-kernel
+    launch per layer, HBM-bound.  The kernel's duration is the CUDA-event time
+    of back-to-back launches divided by the launches (the host issues faster
+    than the kernels run)."""
     from wisp_b200.integrations.vllm.fused_moe import WispMoEState
     L = min(args.layers, 24)
-    B = 1
+    B = batch
     states = []
     for i in range(L):
         st = WispMoEState(masters[i][0], masters[i][1], SHAPE.experts, "resident", dev, i)
@@ -276,7 +352,7 @@ def resident_phase(args, masters, dev, hbm_peak):
         for layer in range(L):
             states[layer].forward(x, w_d[s, layer], ids_d[s, layer], out=out)
     torch.cuda.synchronize()
-    u0 = sum(st.telemetry()["unique_experts"] for st in states)
+    tel0 = [st.telemetry() for st in states]
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for s in range(args.warmup, args.warmup + args.steps):
@@ -285,12 +361,19 @@ def resident_phase(args, masters, dev, hbm_peak):
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
-    ubytes = (sum(st.telemetry()["unique_experts"] for st in states) - u0) * SHAPE.expert_bytes
-    gbs = ubytes / (ms * 1e-3) / 1e9
+    tel1 = [st.telemetry() for st in states]
+    unique = sum(t1["unique_experts"] - t0["unique_experts"] for t0, t1 in zip(tel0, tel1))
+    launches = sum(t1["kernel_launches"] - t0["kernel_launches"] for t0, t1 in zip(tel0, tel1))
+    nbytes = algorithmic_bytes(unique, B * L * args.steps, launches)
+    gbs = nbytes / (ms * 1e-3) / 1e9
     for st in states:
         st.close()
+    torch.cuda.empty_cache()
     return {"layers": L, "batch": B, "tok_s_per_layer_stack": B * args.steps / (ms * 1e-3),
-            "us_per_layer": ms * 1e3 / (args.steps * L), "hbm_gbs": gbs, "hbm_peak_gbs": hbm_peak,
+            "us_per_layer": ms * 1e3 / (args.steps * L), "launches": launches,
+            "us_per_launch": ms * 1e3 / max(launches, 1),
+            "bytes_per_launch": nbytes / max(launches, 1), "unique_experts_per_launch":
+            unique / max(launches, 1), "hbm_gbs": gbs, "hbm_peak_gbs": hbm_peak,
             "frac": gbs / hbm_peak}
 
 
@@ -310,7 +393,9 @@ def run_reference(args):
     scratch = [(torch.empty(C, 2 * I, H, dtype=torch.bfloat16), torch.empty(C, H, I, dtype=torch.bfloat16))
                for _ in range(sample_layers)]
     pagers = [PagerOracle(E, C) for _ in range(sample_layers)]
-    ids_np, w_np = routing(args.warmup + args.steps, sample_layers, B)
+    # a trace long enough for the time-bounded sample (config 2 decodes 512 tokens)
+    n_trace = args.warmup + max(args.steps, 512)
+    ids_np, w_np = routing(n_trace, sample_layers, B)
     x = wl.hidden_states(B, H, seed=0).float()
 
     def layer_fwd(li, s):
@@ -346,7 +431,7 @@ def run_reference(args):
             layer_fwd(li, s)
         done += 1
         s += 1
-        if time.perf_counter() - t0 > args.cpu_sample_s or s >= args.warmup + args.steps:
+        if time.perf_counter() - t0 > args.cpu_sample_s or s >= n_trace:
             break
     dt = time.perf_counter() - t0
     per_layer = dt / (done * sample_layers)
@@ -375,6 +460,8 @@ def main():
         return
     line = run_wisp(args)
     if rank == 0:
+        if args.gpus == 1 and args.cpu_sample_s > 0:
+            line["cpu_baseline"] = run_reference(args)
         print(json.dumps(line))
 
 

@@ -127,6 +127,13 @@ WISP_API int wisp_layer_buffers(wisp_layer *layer, void **scratch_w13, void **sc
 WISP_API int wisp_get_telemetry(wisp_layer *layer, int64_t *out4);
 
 /*
+ * Number of CUDA kernels this layer has launched so far, on every path (one
+ * per asynchronous forward; pager plus two per token group on the synchronous
+ * path).  No counterpart in the reference; used to account for launches.
+ */
+WISP_API int wisp_get_launch_count(wisp_layer *layer, int64_t *out);
+
+/*
  * Wait until every forward issued on this layer has finished (kernels and
  * page-ins) and return the first error any of them hit since the last check
  * (WISP_OK if none).  wisp_moe_forward returns before its work runs; a

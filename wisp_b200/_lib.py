@@ -52,6 +52,7 @@ SIGNATURES = {
     "wisp_layer_buffers": (ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                           ctypes.POINTER(_vp)]),
     "wisp_get_telemetry": (ctypes.c_int, [_vp, _p64]),
+    "wisp_get_launch_count": (ctypes.c_int, [_vp, _p64]),
     "wisp_layer_sync": (ctypes.c_int, [_vp]),
     "wisp_layer_config": (ctypes.c_int, [_vp, _c_int32, _c_int64]),
     "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,

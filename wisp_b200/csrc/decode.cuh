@@ -25,6 +25,8 @@ struct GroupCompute {
 
 // Launch the two decode kernels for one token group; grid y = max_nu CTAs per
 // row block (CTAs beyond the device count n_u exit at once).
+// Launches kDecodeKernelsPerGroup kernels: gate-up + SiLU-mul, then down + combine.
+constexpr int kDecodeKernelsPerGroup = 2;
 int launch_decode_group(const GroupCompute &g, int max_nu, cudaStream_t stream);
 
 }  // namespace wisp

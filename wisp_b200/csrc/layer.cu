@@ -102,6 +102,7 @@ struct wisp_layer {
     unsigned int *d_bar = nullptr;
     unsigned int *d_flow = nullptr;  // forward-kernel dataflow words (kFlowWords)
     int kparity = 0;                 // parity of the forward-kernel launches
+    int64_t launches = 0;            // kernels this layer launched (all paths)
     // per-call workspace, grown on demand
     int wsT = -1, wsK = 0;
     int32_t *d_slots = nullptr, *d_grp_start = nullptr, *d_grp_nu = nullptr, *d_grp_nhit = nullptr,
@@ -478,6 +479,7 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
     WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
     rc = launch_pager(p, stream);
     if (rc) return rc;
+    ++L->launches;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_pager, stream));
     WISP_CUDA_TRY(cudaEventSynchronize(L->ev_pager));
     const int status = ((volatile int32_t *)L->h_mb)[0];
@@ -544,6 +546,7 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
             gc.t1 = t1;
             rc = launch_decode_group(gc, nu[g], stream);
             if (rc) return rc;
+            L->launches += kDecodeKernelsPerGroup;
         }
         WISP_CUDA_TRY(cudaEventRecord(L->ev_group[g], stream));
     }
@@ -605,6 +608,7 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
         return rc;
     }
     L->kparity ^= 1;
+    ++L->launches;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
     if (paged) engine_for(L->dev)->submit(L, fp.pg.seq, T, slot);
     return WISP_OK;
@@ -916,6 +920,13 @@ int wisp_get_telemetry(wisp_layer *L, int64_t *out4) {
     out4[1] = hdr[2];
     out4[2] = hdr[2] * (L->b13 + L->b2);
     out4[3] = hdr[6];
+    return WISP_OK;
+}
+
+int wisp_get_launch_count(wisp_layer *L, int64_t *out) {
+    if (!L || !out) return fail(WISP_ERR_INVALID, "wisp_get_launch_count: NULL argument");
+    std::lock_guard<std::mutex> lk(L->mu);
+    *out = L->launches;
     return WISP_OK;
 }
 

@@ -291,11 +291,13 @@ class WispMoEState:
 
     def telemetry(self) -> dict:
         """Cumulative counters (synchronises): token groups run, misses, page-in
-        bytes, unique experts read summed over groups."""
+        bytes, unique experts read summed over groups, kernels launched."""
         info = (ctypes.c_int64 * 4)()
         _lib.check(_lib.lib().wisp_get_telemetry(self._h, info))
+        n = ctypes.c_int64(0)
+        _lib.check(_lib.lib().wisp_get_launch_count(self._h, ctypes.byref(n)))
         return {"groups": info[0], "misses": info[1], "pagein_bytes": info[2],
-                "unique_experts": info[3]}
+                "unique_experts": info[3], "kernel_launches": n.value}
 
     def configure(self, *, asynchronous: bool | None = None, wait_ns: int | None = None,
                   drop_pageins: int | None = None) -> None:
