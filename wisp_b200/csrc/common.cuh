@@ -35,16 +35,54 @@ __device__ __forceinline__ float round_bf16(float v) {
 }
 
 // 8 bf16 (one 16-byte vector) dotted with 8 bf16, fp32 FMA chain in element order.
-__device__ __forceinline__ float dot8(const uint4 &w, const uint4 &x, float acc) {
-    acc = fmaf(bf16lo(w.x), bf16lo(x.x), acc);
-    acc = fmaf(bf16hi(w.x), bf16hi(x.x), acc);
-    acc = fmaf(bf16lo(w.y), bf16lo(x.y), acc);
-    acc = fmaf(bf16hi(w.y), bf16hi(x.y), acc);
-    acc = fmaf(bf16lo(w.z), bf16lo(x.z), acc);
-    acc = fmaf(bf16hi(w.z), bf16hi(x.z), acc);
-    acc = fmaf(bf16lo(w.w), bf16lo(x.w), acc);
-    acc = fmaf(bf16hi(w.w), bf16hi(x.w), acc);
+// acc += w[0]*x[0] + ... + w[7]*x[7] as an FMA chain in element order (low
+// half of each 32-bit word first).  fma.rn.f32.bf16 multiplies the bf16
+// operands exactly (an 8-bit x 8-bit significand product fits in fp32) and
+// rounds once, so each step equals fmaf on the operands widened to fp32; it
+// needs no widening instructions.
+__device__ __forceinline__ float fma2_bf16(uint32_t w, uint32_t x, float acc) {
+    asm("{\n .reg .b16 wl, wh, xl, xh;\n mov.b32 {wl, wh}, %1;\n mov.b32 {xl, xh}, %2;\n"
+        " fma.rn.f32.bf16 %0, wl, xl, %0;\n fma.rn.f32.bf16 %0, wh, xh, %0;\n}"
+        : "+f"(acc)
+        : "r"(w), "r"(x));
     return acc;
+}
+__device__ __forceinline__ float dot8(const uint4 &w, const uint4 &x, float acc) {
+    acc = fma2_bf16(w.x, x.x, acc);
+    acc = fma2_bf16(w.y, x.y, acc);
+    acc = fma2_bf16(w.z, x.z, acc);
+    acc = fma2_bf16(w.w, x.w, acc);
+    return acc;
+}
+
+// Activation element as stored.  The all-ones bf16 pattern (a NaN) marks an
+// element the one-launch forward has not written yet, so a result with that
+// pattern is stored as the canonical NaN instead (every path does the same).
+constexpr unsigned short kActEmpty = 0xFFFFu;
+__device__ __forceinline__ __nv_bfloat16 act_value(float v) {
+    __nv_bfloat16 b = __float2bfloat16_rn(v);
+    if (__bfloat16_as_ushort(b) == kActEmpty) b = __ushort_as_bfloat16((unsigned short)0x7FFFu);
+    return b;
+}
+// A 2-byte store other SMs poll for (relaxed, device scope: no data race).
+__device__ __forceinline__ void st_relaxed_bf16(__nv_bfloat16 *p, __nv_bfloat16 v) {
+    asm volatile("st.relaxed.gpu.global.b16 [%0], %1;" ::"l"(p), "h"(__bfloat16_as_ushort(v)) : "memory");
+}
+// 16-byte load that always reads the coherent level (polling other SMs' stores).
+__device__ __forceinline__ uint4 ld_volatile16(const void *p) {
+    uint4 r;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+__device__ __forceinline__ bool half_empty(uint32_t w) {
+    return (w & 0xFFFFu) == kActEmpty || (w >> 16) == kActEmpty;
+}
+// Any of the eight bf16 elements still the "not written" pattern?
+__device__ __forceinline__ bool has_empty(const uint4 &v) {
+    return half_empty(v.x) | half_empty(v.y) | half_empty(v.z) | half_empty(v.w);
 }
 
 // Streaming 16-byte load for weights read once per forward (no L1 allocation).

@@ -2,31 +2,34 @@
 //
 //   phase 0  block 0 runs the LRU pager (pager_body) for every token group of
 //            the call.  Meanwhile, when the call's experts fit the cap (one
-//            group, decode sizes), the other blocks already run phase 1 for
-//            the experts that were resident before the call: those are exactly
-//            the pager's hits, they keep their slots, and block 0 writes the
-//            new expert map back only after the first grid barrier;
-//   then, per group g (work is handed out per warp, round-robin):
-//   phase 1  gate-up GEMV + SiLU-mul, unit = one row pair of one unique
-//            expert (the rest of them, after a speculative start); a unit of
-//            an expert paged in during this call first waits until the slot's
-//            generation flag (written by the copy stream after the two
-//            copies) reaches the generation the pager assigned;
-//   phase 2  down GEMV x routing weight, unit = four rows of one expert; the
-//            last unit of a row quad to finish (arrival counter) sums the
-//            group's tokens over k in routing order for those rows;
-//            between groups block 0 publishes "group g done" to mapped host
-//            memory, which lets the host copy thread overwrite slots g read.
+//            group, decode sizes), the other blocks already compute the
+//            experts that were resident before the call: those are exactly
+//            the pager's hits and keep their slots; block 0 writes the new
+//            expert map back only after every block has read the old one;
+//   units    gate-up GEMV + SiLU-mul, unit = one row pair of one unique
+//            expert; down GEMV x routing weight, unit = four rows of one
+//            expert.  A unit of an expert paged in during this call first
+//            waits until the slot's generation flag (written by the copy
+//            stream after the two copies) reaches the generation the pager
+//            assigned.  The last down unit of a row quad to finish (arrival
+//            counter) sums the group's tokens over k in routing order for
+//            those rows.
 //
-// Decode-sized groups keep their unique-expert lists in shared memory and
-// each warp loads the weights of its next unit while computing the current
-// one; larger groups use the generic bodies of moe_body.cuh.  The arithmetic
-// per (token, expert) pair is the same everywhere (moe_body.cuh documents it).
+// Decode sizes (FAST): each warp runs one pipelined stream of units - its
+// gate-up units, then its down units - with the weight rows streamed into
+// shared memory by cp.async.bulk; a down unit polls the activation rows it
+// needs (each element is written once per launch over a "not written"
+// pattern, so the element is its own flag: no counters or fences between the
+// phases).  A call of several token groups separates the phases with grid
+// barriers, and between groups block 0 publishes "group g done" to mapped
+// host memory, which lets the host copy thread overwrite slots g read.  Larger
+// shapes use the generic bodies of moe_body.cuh.  The arithmetic per (token,
+// expert) pair is the same everywhere (moe_body.cuh documents it).
 //
-// Every wait (grid barrier, slot flag) is bounded by wait_ns of
-// %globaltimer time; a wait that runs out sets the abort word and the sticky
-// status WISP_ERR_TIMEOUT, every other wait then gives up too, and the
-// kernel returns.
+// Every wait (grid barrier, slot flag, copy, activation poll) is bounded by
+// wait_ns of %globaltimer time; a wait that runs out sets the abort word and
+// the sticky status WISP_ERR_TIMEOUT, every other wait then gives up too, and
+// the kernel returns.
 #include "forward.cuh"
 #include "moe_body.cuh"
 #include "pager_body.cuh"
@@ -111,13 +114,16 @@ struct Meta {
 };
 
 // ---- TMA-fed units (decode sizes) --------------------------------------------
-// Each warp owns kStages shared-memory buffers of kStageBytes with one
+// Each warp owns `nst` (2 or 3) shared-memory stages of kStageBytes with one
 // mbarrier each.  Lane 0 streams a unit's weight rows (contiguous blocks) in
 // with cp.async.bulk; the warp computes from shared memory while the copies of
 // its next units are in flight.  Every mbarrier wait is bounded in time.
-constexpr int kStages = 2;
+constexpr int kMaxStages = 3;
 constexpr int kStageBytes = 8192;  // >= 2 rows x H (gate-up) and 4 rows x I (down), bf16
-constexpr int kPubLane = 31;       // lane that stores and publishes gate-up rows
+constexpr int kPubLane = 31;       // lane that stores gate-up rows
+constexpr int kPairPass = 4;       // (token, k) pairs per pass over a unit's rows
+constexpr int kDownChunk = 4;      // consecutive down units per hand-out
+constexpr int kTraceWarps = 8 + 4 * 1024;  // per-warp records (16 words) start here in the trace buffer
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -151,10 +157,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Per-warp copy pipeline state.
 struct WarpPipe {
-    unsigned char *buf;  // kStages * kStageBytes
-    uint64_t *bar;       // kStages mbarriers
+    unsigned char *buf;  // nst * kStageBytes
+    uint64_t *bar;       // nst mbarriers
     uint32_t phase;      // bit s: parity to wait for on stage s
     uint32_t pending;    // bit s: a copy into stage s has not been waited for
+    int nst;             // stages in use
 };
 
 // Wait for stage s (bounded); on timeout record it and abort.
@@ -178,7 +185,7 @@ __device__ bool pipe_wait(WarpPipe &w, int s, const ForwardParams &fp) {
 // Before leaving on an abort: let the copies still landing in this warp's
 // buffers finish (each wait bounded), so no copy outlives the block.
 __device__ void pipe_drain(WarpPipe &w, const ForwardParams &fp) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < w.nst; ++s) {
         if (!((w.pending >> s) & 1u)) continue;
         const uint32_t par = (w.phase >> s) & 1u;
         const unsigned long long t0 = globaltimer_ns();
@@ -189,7 +196,7 @@ __device__ void pipe_drain(WarpPipe &w, const ForwardParams &fp) {
     w.pending = 0;
 }
 
-// Lane 0 (the caller has established the slot is ready): copy `n` blocks.
+// Lane 0 (the caller has established the slot is ready): copy one or two blocks.
 __device__ __forceinline__ void pipe_issue(WarpPipe &w, int s, const void *src0, uint32_t b0,
                                            const void *src1, uint32_t b1) {
     unsigned char *dst = w.buf + s * kStageBytes;
@@ -199,274 +206,355 @@ __device__ __forceinline__ void pipe_issue(WarpPipe &w, int s, const void *src0,
     if (b1) bulk_g2s(dst + b0, src1, b1, w.bar + s);
 }
 
-// Gate-up units k = (u - u_lo) * I + j, u in [u_lo, m.nu); this warp takes
-// k = wid, wid + nw, ...  Returns false when the kernel is aborting.
-template <int MAXP>
-__device__ bool gateup_units(const GroupCompute &a, const Meta &m, int u_lo, int wid, int nw, int lane,
-                             const ForwardParams &fp, WarpPipe &w, unsigned int *done1) {
+// A warp's share of the units of experts [u0, u1) of the group's lists:
+// gate-up units first (unit k: expert u0 + k / I, row pair k % I; this warp
+// takes k = wid, wid + nw, ...), then down units (unit k: expert u0 + k / nq,
+// rows 4 (k % nq) ..; kDownChunk consecutive units per hand-out, hand-outs
+// round-robin starting with the warp after the one that took the last
+// gate-up unit).  A warp's stream is one pipeline: the copies of its first
+// down units are in flight while its last gate-up units compute.
+struct Stream {
+    int u0;
+    int n_gu, my_gu;  // gate-up units: all / this warp's
+    int n_dn, my_dn;  // down units: all / this warp's
+    int dn_w;         // this warp's place in the down rotation
+    int wid, nw;
+};
+
+__device__ __forceinline__ Stream make_stream(int u0, int u1, bool gu, bool dn, int wid, int nw, int I,
+                                              int nq) {
+    Stream s;
+    s.u0 = u0;
+    s.wid = wid;
+    s.nw = nw;
+    const int ne = u1 > u0 ? u1 - u0 : 0;
+    s.n_gu = gu ? ne * I : 0;
+    s.my_gu = wid < s.n_gu ? (s.n_gu - 1 - wid) / nw + 1 : 0;
+    s.n_dn = dn ? ne * nq : 0;
+    s.dn_w = (wid - s.n_gu % nw + nw) % nw;
+    const int nch = (s.n_dn + kDownChunk - 1) / kDownChunk;
+    int my = 0;
+    if (s.dn_w < nch) {
+        my = ((nch - 1 - s.dn_w) / nw + 1) * kDownChunk;
+        if ((nch - 1 - s.dn_w) % nw == 0) my -= nch * kDownChunk - s.n_dn;  // holds the short last hand-out
+    }
+    s.my_dn = my;
+    return s;
+}
+
+// Down unit d (0-based among this warp's down units) -> unit index.
+__device__ __forceinline__ int down_unit(const Stream &s, int d) {
+    return (s.dn_w + (d / kDownChunk) * s.nw) * kDownChunk + d % kDownChunk;
+}
+
+// One pass of a gate-up unit over P pairs starting at list entry qb.
+template <int P>
+__device__ __forceinline__ void gu_pass(const GroupCompute &a, const Meta &m, int qb, const unsigned char *st,
+                                        int j, int lane) {
     const int H = a.H, I = a.I;
+    const uint4 *gs = reinterpret_cast<const uint4 *>(st);
+    const uint4 *us = reinterpret_cast<const uint4 *>(st + (size_t)H * 2);
+    const __nv_bfloat16 *xp[P];
+#pragma unroll
+    for (int t = 0; t < P; ++t) xp[t] = a.x + (size_t)m.tok[qb + t] * H + lane * 8;
+    float ag[P], au[P];
+#pragma unroll
+    for (int t = 0; t < P; ++t) {
+        ag[t] = 0.f;
+        au[t] = 0.f;
+    }
+#pragma unroll
+    for (int c8 = 0; c8 < kGuChunks; ++c8) {
+        const int c = c8 * 256 + lane * 8;
+        if (c < H) {
+            const uint4 wg = gs[c >> 3], wu = us[c >> 3];
+            uint4 xv[P];
+#pragma unroll
+            for (int t = 0; t < P; ++t) xv[t] = ld_cached16(xp[t] + c8 * 256);
+#pragma unroll
+            for (int t = 0; t < P; ++t) {
+                ag[t] = dot8(wg, xv[t], ag[t]);
+                au[t] = dot8(wu, xv[t], au[t]);
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < P; ++t) {
+        const float g = round_bf16(warp_sum(ag[t]));
+        const float v = round_bf16(warp_sum(au[t]));
+        if (lane == kPubLane) {  // one lane stores every pair's row j
+            const float sg = g / (1.0f + expf(-g));
+            st_relaxed_bf16(a.act + (size_t)m.pair[qb + t] * I + j, act_value(sg * v));
+        }
+    }
+}
+
+// Activation rows of up to kPairPass pairs, kept in registers across the down
+// units of one expert.
+struct ActCache {
+    uint4 v[kPairPass][kDqChunks];
+};
+
+// One pass of a down unit over P pairs starting at list entry qb; `cache`
+// holds the pairs' activation rows when the expert has at most kPairPass pairs.
+template <int P, bool CACHED>
+__device__ __forceinline__ void dn_pass(const GroupCompute &a, const Meta &m, int qb, const unsigned char *st,
+                                        int h0, int nr, int lane, const ActCache &cache) {
+    const int H = a.H, I = a.I;
+    const uint4 *ws = reinterpret_cast<const uint4 *>(st);
+    float acc[4][P];
+#pragma unroll
+    for (int t = 0; t < P; ++t)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][t] = 0.f;
+#pragma unroll
+    for (int c4 = 0; c4 < kDqChunks; ++c4) {
+        const int c = c4 * 256 + lane * 8;
+        if (c < I) {
+            uint4 wv[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) wv[r] = ws[((r < nr ? r : 0) * I + c) >> 3];
+#pragma unroll
+            for (int t = 0; t < P; ++t) {
+                const uint4 av = CACHED ? cache.v[t][c4] : ld_cg16(a.act + (size_t)m.pair[qb + t] * I + c);
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[r][t] = dot8(wv[r], av, acc[r][t]);
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < P; ++t) {
+        const int p = m.pair[qb + t];
+        const float wp = a.topk_w[p];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float sum = warp_sum(acc[r][t]);
+            if (lane == r && r < nr) a.y[(size_t)p * H + h0 + r] = __float2bfloat16_rn(sum * wp);
+        }
+    }
+}
+
+// Until every activation row of expert u's pairs is written (no element still
+// kActEmpty; each element is written once per launch by one 2-byte store), poll
+// this lane's chunks of them (bounded).  With CACHED (at most kPairPass pairs)
+// the rows land in `cache`.  Returns false when the kernel is aborting.
+template <bool CACHED>
+__device__ bool poll_act(const GroupCompute &a, const Meta &m, int q0, int np, int lane,
+                         const ForwardParams &fp, ActCache &cache) {
+    const int I = a.I;
+    unsigned long long t0 = 0;
+    volatile unsigned int *vabort = fp.bar + kBarAbort;
+    for (int iter = 0;; ++iter) {
+        bool full = true;
+        if (CACHED) {
+#pragma unroll
+            for (int t = 0; t < kPairPass; ++t)
+                if (t < np)
+#pragma unroll
+                    for (int c4 = 0; c4 < kDqChunks; ++c4) {
+                        const int c = c4 * 256 + lane * 8;
+                        if (c < I) {
+                            cache.v[t][c4] = ld_volatile16(a.act + (size_t)m.pair[q0 + t] * I + c);
+                            full &= !has_empty(cache.v[t][c4]);
+                        }
+                    }
+        } else {
+            for (int t = 0; t < np; ++t)
+#pragma unroll
+                for (int c4 = 0; c4 < kDqChunks; ++c4) {
+                    const int c = c4 * 256 + lane * 8;
+                    if (c < I) full &= !has_empty(ld_volatile16(a.act + (size_t)m.pair[q0 + t] * I + c));
+                }
+        }
+        if (__all_sync(0xffffffffu, full)) return true;
+        int stop = 0;
+        if (lane == 0) {
+            if (iter == 0) t0 = globaltimer_ns();
+            if (*vabort) {
+                stop = 1;
+            } else if ((long long)(globaltimer_ns() - t0) > fp.wait_ns) {
+                set_status(fp.bar, WISP_ERR_TIMEOUT);
+                atomicExch(fp.bar + kBarAbort, 1u);
+                stop = 1;
+            }
+        }
+        if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+        __nanosleep(128);
+    }
+}
+
+// Run a warp's stream.  With `dataflow`, a down unit first polls until its
+// expert's activation rows are complete (its W2 copy already in flight);
+// without it the caller separates the phases with a grid barrier.  Down units
+// store the weighted y; the row-quad arrivals are made later (arrive_stream).
+// Returns false when the kernel is aborting.
+// Optional per-warp trace (debug; `wtr` null when off): [0] start, [1] first
+// unit's data ready, [2] last gate-up unit's data ready, [3] all units done,
+// [4] ns in copy waits, [5] ns in activation polls, [6] units; %globaltimer.
+__device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S, int lane,
+                           const ForwardParams &fp, WarpPipe &w, bool dataflow,
+                           unsigned long long *wtr = nullptr) {
+    const int H = a.H, I = a.I;
+    const int nq = (H + 3) / 4;
     const uint32_t rowb = (uint32_t)H * 2;
-    const long total = (long)(m.nu - u_lo) * I;
-    auto issue = [&](long k, int s) -> bool {
-        const int u = u_lo + (int)(k / I), j = (int)(k % I);
+    const int total = S.my_gu + S.my_dn;
+    if (total == 0) return true;
+    unsigned long long t_copy = 0, t_act = 0;
+    if (wtr && lane == 0) {
+        wtr[0] = globaltimer_ns();
+        wtr[6] = (unsigned long long)total;
+    }
+    // unit i of this warp -> expert u, and row pair j (gate-up) or row quad q (down)
+    auto describe = [&](int i, int &u, int &r) -> bool {
+        if (i < S.my_gu) {
+            const int k = S.wid + i * S.nw;
+            const int e = k / I;
+            u = S.u0 + e;
+            r = k - e * I;
+            return true;
+        }
+        const int k = down_unit(S, i - S.my_gu);
+        const int e = k / nq;
+        u = S.u0 + e;
+        r = k - e * nq;
+        return false;
+    };
+    auto issue = [&](int i, int s) -> bool {
+        int u, r;
+        const bool gu = describe(i, u, r);
         if (m.gen[u] != 0) {  // expert paged in during this call: its slot must have landed
             int ok = 1;
             if (lane == 0) ok = wait_slot(fp.slot_ready, m.slot[u], (uint32_t)m.gen[u], fp.bar, fp.wait_ns);
             if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
         }
         if (lane == 0) {
-            const __nv_bfloat16 *g = a.w13 + (size_t)m.slot[u] * (size_t)(2 * I) * H + (size_t)j * H;
-            pipe_issue(w, s, g, rowb, g + (size_t)I * H, rowb);
+            if (gu) {
+                const __nv_bfloat16 *g = a.w13 + (size_t)m.slot[u] * (size_t)(2 * I) * H + (size_t)r * H;
+                pipe_issue(w, s, g, rowb, g + (size_t)I * H, rowb);
+            } else {
+                const int nr = min(4, H - 4 * r);
+                pipe_issue(w, s, a.w2 + (size_t)m.slot[u] * (size_t)H * I + (size_t)(4 * r) * I,
+                           (uint32_t)nr * I * 2, nullptr, 0);
+            }
         }
         w.pending |= 1u << s;
         return true;
     };
     bool ok = true;
-    for (int s = 0; s < kStages && ok; ++s) {
-        const long k = wid + (long)s * nw;
-        if (k < total) ok = issue(k, s);
-    }
-    // publication of the previous unit's rows, one unit late: by then its stores
-    // have completed and the fence costs little
-    // (the stores and the fence are on kPubLane, not on lane 0 which issues the
-    // copies: a fence must not wait for this warp's copies in flight)
-    int pub_u = -1;
-    unsigned pub_n = 0;
-    auto publish = [&]() {
-        if (done1 && pub_n && lane == kPubLane) {
-            __threadfence();
-            atomicAdd(done1 + pub_u, pub_n);
-        }
-        pub_n = 0;
-    };
-    long i = 0;
-    for (long k = wid; ok && k < total; k += nw, ++i) {
-        const int s = (int)(i % kStages);
-        if (!pipe_wait(w, s, fp)) {
-            ok = false;
-            break;
-        }
-        publish();
-        const int u = u_lo + (int)(k / I), j = (int)(k % I);
-        const uint4 *gs = reinterpret_cast<const uint4 *>(w.buf + s * kStageBytes);
-        const uint4 *us = reinterpret_cast<const uint4 *>(w.buf + s * kStageBytes + rowb);
-        const int q0 = m.off[u], q1 = m.off[u + 1];
-        for (int qb = q0; qb < q1; qb += MAXP) {
-            const int np = min(MAXP, q1 - qb);
-            float ag[MAXP], au[MAXP];
-#pragma unroll
-            for (int t = 0; t < MAXP; ++t) {
-                ag[t] = 0.f;
-                au[t] = 0.f;
+    for (int s = 0; s < w.nst && ok; ++s)
+        if (s < total) ok = issue(s, s);
+    ActCache cache;
+    int cache_u = -1, ready_u = -1;
+    int s = 0;
+    for (int i = 0; ok && i < total; ++i) {
+        int u, r;
+        const bool gu = describe(i, u, r);
+        const int q0 = m.off[u], q1 = m.off[u + 1], np = q1 - q0;
+        const unsigned char *st = w.buf + s * kStageBytes;
+        if (gu) {
+            const unsigned long long tw = wtr ? globaltimer_ns() : 0;
+            if (!pipe_wait(w, s, fp)) {
+                ok = false;
+                break;
             }
+            if (wtr) {
+                const unsigned long long now = globaltimer_ns();
+                t_copy += now - tw;
+                if (i == 0 && lane == 0) wtr[1] = now;
+                if (i + 1 == S.my_gu && lane == 0) wtr[2] = now;
+            }
+            int qb = q0;
+            for (; qb + kPairPass <= q1; qb += kPairPass) gu_pass<kPairPass>(a, m, qb, st, r, lane);
+            switch (q1 - qb) {
+                case 1: gu_pass<1>(a, m, qb, st, r, lane); break;
+                case 2: gu_pass<2>(a, m, qb, st, r, lane); break;
+                case 3: gu_pass<3>(a, m, qb, st, r, lane); break;
+                default: break;
+            }
+        } else {
+            const bool cached = np <= kPairPass;
+            if (dataflow && u != ready_u) {
+                const unsigned long long ta = wtr ? globaltimer_ns() : 0;
+                if (!(cached ? poll_act<true>(a, m, q0, np, lane, fp, cache)
+                             : poll_act<false>(a, m, q0, np, lane, fp, cache))) {
+                    ok = false;
+                    break;
+                }
+                if (wtr) t_act += globaltimer_ns() - ta;
+                ready_u = u;
+                if (cached) cache_u = u;
+            }
+            if (cached && u != cache_u) {  // this expert's activation rows, reused by its next units
 #pragma unroll
-            for (int c8 = 0; c8 < kGuChunks; ++c8) {
-                const int c = c8 * 256 + lane * 8;
-                if (c < H) {
-                    const uint4 wg = gs[c >> 3], wu = us[c >> 3];
+                for (int t = 0; t < kPairPass; ++t)
+                    if (t < np)
 #pragma unroll
-                    for (int t = 0; t < MAXP; ++t) {
-                        if (t < np) {
-                            const uint4 xv = ld_cached16(a.x + (size_t)m.tok[qb + t] * H + c);
-                            ag[t] = dot8(wg, xv, ag[t]);
-                            au[t] = dot8(wu, xv, au[t]);
+                        for (int c4 = 0; c4 < kDqChunks; ++c4) {
+                            const int c = c4 * 256 + lane * 8;
+                            if (c < I) cache.v[t][c4] = ld_cg16(a.act + (size_t)m.pair[q0 + t] * I + c);
                         }
-                    }
-                }
+                cache_u = u;
             }
-#pragma unroll
-            for (int t = 0; t < MAXP; ++t) {
-                if (t < np) {
-                    const float g = round_bf16(warp_sum(ag[t]));
-                    const float v = round_bf16(warp_sum(au[t]));
-                    if (lane == kPubLane) {  // one lane stores every pair's row j and publishes them
-                        const float sg = g / (1.0f + expf(-g));
-                        a.act[(size_t)m.pair[qb + t] * I + j] = __float2bfloat16_rn(sg * v);
-                    }
+            const unsigned long long tw = wtr ? globaltimer_ns() : 0;
+            if (!pipe_wait(w, s, fp)) {
+                ok = false;
+                break;
+            }
+            if (wtr) {
+                t_copy += globaltimer_ns() - tw;
+                if (i == 0 && lane == 0) wtr[1] = globaltimer_ns();
+            }
+            const int h0 = 4 * r, nr = min(4, H - h0);
+            if (cached) {
+                switch (np) {
+                    case 1: dn_pass<1, true>(a, m, q0, st, h0, nr, lane, cache); break;
+                    case 2: dn_pass<2, true>(a, m, q0, st, h0, nr, lane, cache); break;
+                    case 3: dn_pass<3, true>(a, m, q0, st, h0, nr, lane, cache); break;
+                    case 4: dn_pass<4, true>(a, m, q0, st, h0, nr, lane, cache); break;
+                    default: break;
+                }
+            } else {
+                int qb = q0;
+                for (; qb + kPairPass <= q1; qb += kPairPass)
+                    dn_pass<kPairPass, false>(a, m, qb, st, h0, nr, lane, cache);
+                switch (q1 - qb) {
+                    case 1: dn_pass<1, false>(a, m, qb, st, h0, nr, lane, cache); break;
+                    case 2: dn_pass<2, false>(a, m, qb, st, h0, nr, lane, cache); break;
+                    case 3: dn_pass<3, false>(a, m, qb, st, h0, nr, lane, cache); break;
+                    default: break;
                 }
             }
         }
-        pub_u = u;
-        pub_n = (unsigned)(q1 - q0);
         __syncwarp();
-        const long kn = k + (long)kStages * nw;
-        if (kn < total) ok = issue(kn, s);
+        if (i + w.nst < total) ok = issue(i + w.nst, s);
+        s = (s + 1 == w.nst) ? 0 : s + 1;
     }
     if (!ok) {
         pipe_drain(w, fp);
         return false;
     }
-    publish();
+    if (wtr && lane == 0) {
+        wtr[3] = globaltimer_ns();
+        wtr[4] = t_copy;
+        wtr[5] = t_act;
+    }
     return true;
 }
 
-// The last of the nu units of row quad q to finish sums the group's tokens.
-__device__ __forceinline__ void quad_arrive(const GroupCompute &a, int q, int nu, int lane) {
+// Row-quad arrivals of a warp's down units (after their y stores): one fence,
+// then one lane per unit; the last of the nu arrivals on a quad sums the
+// group's tokens over k in routing order for its rows.
+__device__ void arrive_stream(const GroupCompute &a, const Stream &S, int nu, int lane) {
+    if (S.my_dn == 0) return;
+    const int nq = (a.H + 3) / 4;
     __threadfence();
     __syncwarp();
-    int last = 0;
-    if (lane == 0) last = (atomicAdd(&a.counters[q], 1) == nu - 1);
-    if (__shfl_sync(0xffffffffu, last, 0)) {
-        __threadfence();
-        combine_rows(a, q * 4, 4, lane, 32);
-        if (lane == 0) a.counters[q] = 0;
-    }
-}
-
-// Wait (lane 0, bounded) until every gate-up row of expert u is published.
-__device__ bool wait_act(const unsigned int *done1, int u, unsigned int need, const ForwardParams &fp,
-                         int lane) {
-    int ok = 1;
-    if (lane == 0) {
-        volatile const unsigned int *f = done1 + u;
-        if (*f < need) {
-            volatile unsigned int *vabort = fp.bar + kBarAbort;
-            const unsigned long long t0 = globaltimer_ns();
-            while (*f < need) {
-                if (*vabort) {
-                    ok = 0;
-                    break;
-                }
-                if ((long long)(globaltimer_ns() - t0) > fp.wait_ns) {
-                    set_status(fp.bar, WISP_ERR_TIMEOUT);
-                    atomicExch(fp.bar + kBarAbort, 1u);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(64);
-            }
-        }
-        __threadfence();
-    }
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
-// Down units k = u * nq + q (four rows h0 = 4q.. of expert u, one contiguous
-// block of W2) for u < m.nu.  Units go out in chunks of kDownChunk
-// consecutive units (mostly one expert, whose activation rows then stay in
-// registers), chunks round-robin over the warps.  With `done1`, a unit first
-// waits until its expert's activations are complete (its W2 copy is already
-// in flight).  The weighted y of every unit goes to global memory; at the end
-// the warp fences once and its lanes arrive on the row quads' counters in
-// parallel; the last arrival of a quad sums the group's tokens over k in
-// routing order for those rows.
-constexpr int kDownChunk = 4;
-template <int MAXQ>
-__device__ bool down_units(const GroupCompute &a, const Meta &m, int wid, int nw, int lane,
-                           const ForwardParams &fp, WarpPipe &w, const unsigned int *done1) {
-    const int H = a.H, I = a.I;
-    const int nq = (H + 3) / 4;
-    const long total = (long)m.nu * nq;
-    // the i-th unit of this warp (may be >= total past the last one)
-    auto unit_of = [&](long i) -> long {
-        return ((long)wid + (i / kDownChunk) * nw) * kDownChunk + (i % kDownChunk);
-    };
-    long count = 0;
-    while (unit_of(count) < total) ++count;  // at most a few chunks per warp
-    if (count == 0) return true;
-    // a unit of an expert paged in during this call reads its slot only after
-    // the page-in has landed
-    auto issue = [&](long i, int s) -> bool {
-        const long k = unit_of(i);
-        const int u = (int)(k / nq), q = (int)(k % nq);
-        const int nr = min(4, H - 4 * q);
-        if (m.gen[u] != 0) {
-            int rdy = 1;
-            if (lane == 0) rdy = wait_slot(fp.slot_ready, m.slot[u], (uint32_t)m.gen[u], fp.bar, fp.wait_ns);
-            if (!__shfl_sync(0xffffffffu, rdy, 0)) return false;
-        }
-        if (lane == 0)
-            pipe_issue(w, s, a.w2 + (size_t)m.slot[u] * (size_t)H * I + (size_t)(4 * q) * I,
-                       (uint32_t)nr * I * 2, nullptr, 0);
-        w.pending |= 1u << s;
-        return true;
-    };
-    bool ok = true;
-    for (int s = 0; s < kStages && ok; ++s)
-        if (s < count) ok = issue(s, s);
-    uint4 act[MAXQ][kDqChunks];
-    int act_u = -1;
-    for (long i = 0; ok && i < count; ++i) {
-        const int s = (int)(i % kStages);
-        const long k = unit_of(i);
-        const int u = (int)(k / nq), q = (int)(k % nq), h0 = 4 * q;
-        const int q0 = m.off[u], q1 = m.off[u + 1];
-        if (done1 && u != act_u && !wait_act(done1, u, (unsigned)(I * (q1 - q0)), fp, lane)) {
-            ok = false;
-            break;
-        }
-        const bool cached = (q1 - q0) <= MAXQ;
-        if (cached && u != act_u) {  // this expert's activation rows, reused by its next quads
-#pragma unroll
-            for (int t = 0; t < MAXQ; ++t)
-                if (t < q1 - q0)
-#pragma unroll
-                    for (int c4 = 0; c4 < kDqChunks; ++c4) {
-                        const int c = c4 * 256 + lane * 8;
-                        if (c < I) act[t][c4] = ld_cg16(a.act + (size_t)m.pair[q0 + t] * I + c);
-                    }
-        }
-        act_u = u;
-        if (!pipe_wait(w, s, fp)) {
-            ok = false;
-            break;
-        }
-        const int nr = min(4, H - h0);
-        const uint4 *ws = reinterpret_cast<const uint4 *>(w.buf + s * kStageBytes);
-        for (int qb = q0; qb < q1; qb += MAXQ) {
-            const int np = min(MAXQ, q1 - qb);
-            float acc[4][MAXQ];
-#pragma unroll
-            for (int t = 0; t < MAXQ; ++t)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) acc[r][t] = 0.f;
-#pragma unroll
-            for (int c4 = 0; c4 < kDqChunks; ++c4) {
-                const int c = c4 * 256 + lane * 8;
-                if (c < I) {
-                    uint4 wv[4];
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) wv[r] = ws[((r < nr ? r : 0) * I + c) >> 3];
-#pragma unroll
-                    for (int t = 0; t < MAXQ; ++t) {
-                        if (t < np) {
-                            const uint4 av =
-                                cached ? act[t][c4] : ld_cg16(a.act + (size_t)m.pair[qb + t] * I + c);
-#pragma unroll
-                            for (int r = 0; r < 4; ++r) acc[r][t] = dot8(wv[r], av, acc[r][t]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < MAXQ; ++t) {
-                if (t < np) {
-                    const int p = m.pair[qb + t];
-                    const float wp = a.topk_w[p];
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const float sum = warp_sum(acc[r][t]);
-                        if (lane == r && r < nr) a.y[(size_t)p * H + h0 + r] = __float2bfloat16_rn(sum * wp);
-                    }
-                }
-            }
-        }
-        __syncwarp();
-        if (i + kStages < count) ok = issue(i + kStages, s);
-    }
-    if (!ok) {
-        pipe_drain(w, fp);
-        return false;
-    }
-    // arrivals: one fence, then one lane per unit
-    __threadfence();
-    __syncwarp();
-    for (long ib = 0; ib < count; ib += 32) {
-        const long i = ib + lane;
+    for (int db = 0; db < S.my_dn; db += 32) {
+        const int d = db + lane;
         int last = 0, q = 0;
-        if (i < count) {
-            q = (int)(unit_of(i) % nq);
-            last = (atomicAdd(&a.counters[q], 1) == m.nu - 1);
+        if (d < S.my_dn) {
+            q = down_unit(S, d) % nq;
+            last = (atomicAdd(&a.counters[q], 1) == nu - 1);
         }
         unsigned todo = __ballot_sync(0xffffffffu, last);
         if (todo) __threadfence();
@@ -478,7 +566,20 @@ __device__ bool down_units(const GroupCompute &a, const Meta &m, int wid, int nw
             if (lane == 0) a.counters[ql] = 0;
         }
     }
-    return true;
+}
+
+// The last of the nu units of row quad q to finish sums the group's tokens
+// (generic variant).
+__device__ __forceinline__ void quad_arrive(const GroupCompute &a, int q, int nu, int lane) {
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = (atomicAdd(&a.counters[q], 1) == nu - 1);
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+        __threadfence();
+        combine_rows(a, q * 4, 4, lane, 32);
+        if (lane == 0) a.counters[q] = 0;
+    }
 }
 
 // Generic (non-pipelined) bodies for groups beyond the shared-memory lists.
@@ -660,10 +761,10 @@ __device__ bool block_wait_word(const unsigned int *word, unsigned int want, con
 }
 
 // FAST: decode sizes (every group's lists fit in shared memory, H <= 2048,
-// I <= 1024): TMA-fed warp units, a speculative start, and for a call that
-// forms one token group no grid barrier at all (dataflow counters).
-// Otherwise the generic bodies with grid barriers between phases.  The host
-// picks the variant from the shapes alone.
+// I <= 1024): TMA-fed warp streams, a speculative start, and for a call that
+// forms one token group no grid barrier at all (down units poll the
+// activation rows they need).  Otherwise the generic bodies with grid
+// barriers between phases.  The host picks the variant from the shapes alone.
 template <int MAXP, bool FAST>
 __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(const __grid_constant__ ForwardParams a) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -673,7 +774,7 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
     const int nwarps = gridDim.x * kWarpsPerBlock;
     const int gw = blockIdx.x * kWarpsPerBlock + warp;
     const PagerParams &pg = a.pg;
-    unsigned int *done1 = a.flow + kFlowDone1 + a.epoch * kFlowMaxU;
+    const int H = a.gc.H, I = a.gc.I, nq = (H + 3) / 4;
     unsigned long long *tr = a.trace;
 #define WISP_TRACE(slot)                                                                 \
     do {                                                                                 \
@@ -685,16 +786,20 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
     } while (0)
     WISP_TRACE(0);
     WISP_TRACE0(0);
+    // the next launch's activation buffer: every element "not written yet"
+    for (long i = (long)blockIdx.x * kFwdThreads + tid; i < a.act_reset_words; i += (long)gridDim.x * kFwdThreads)
+        a.act_reset[i] = 0xFFFFFFFFu;
 
     // per-warp copy pipelines (FAST variant); buffers overlay the pager's shared
     // memory, which block 0 is done with before its first copy
-    __shared__ __align__(8) uint64_t s_bars[kWarpsPerBlock][kStages];
+    __shared__ __align__(8) uint64_t s_bars[kWarpsPerBlock][kMaxStages];
     WarpPipe pipe{};
     if (FAST) {
-        pipe.buf = smem + (size_t)warp * kStages * kStageBytes;
+        pipe.nst = a.stages;
+        pipe.buf = smem + (size_t)warp * a.stages * kStageBytes;
         pipe.bar = s_bars[warp];
         if (lane == 0) {
-            for (int st = 0; st < kStages; ++st) mbar_init(pipe.bar + st, 1);
+            for (int st = 0; st < a.stages; ++st) mbar_init(pipe.bar + st, 1);
             fence_proxy_async();
         }
         __syncwarp();
@@ -703,15 +808,12 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
     // ---- phase 0 ------------------------------------------------------------------
     // block 0: pager, publish its outputs, wait until no block still reads the
     // pre-call expert map, write the new state back.  Other blocks: read the
-    // pre-call map (speculation lists), say so, run gate-up for the experts
-    // that were resident before the call.
-    bool spec_here = false;
+    // pre-call map (speculation lists), say so, and run the gate-up and down
+    // units of the experts that were resident before the call (their row-quad
+    // arrivals wait until the call's expert count is known).
+    Stream spec{};
     if (blockIdx.x == 0) {
-        if (tid == 0) {  // the counters the next launch uses start at zero
-            a.flow[kFlowSpecRead + (a.epoch ^ 1)] = 0;
-        }
-        for (int i = tid; i < kFlowMaxU; i += kFwdThreads)
-            a.flow[kFlowDone1 + (a.epoch ^ 1) * kFlowMaxU + i] = 0;
+        if (tid == 0) a.flow[kFlowSpecRead + (a.epoch ^ 1)] = 0;  // the next launch's count starts at zero
         pager_body(pg, smem);
         if (tid == 0) {
             __threadfence();
@@ -722,6 +824,7 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
         pager_finish(pg, smem, a.publish != 0);
         WISP_TRACE0(2);
     } else {
+        bool spec_here = false;
         if (FAST) spec_here = build_spec_meta(a, meta, reinterpret_cast<int *>(smem));
         __syncthreads();
         if (tid == 0) {
@@ -732,8 +835,9 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
             GroupCompute gc = a.gc;
             gc.t0 = 0;
             gc.t1 = pg.T;
-            gateup_units<MAXP>(gc, meta, 0, gw - kWarpsPerBlock, nwarps - kWarpsPerBlock, lane, a, pipe,
-                               done1);
+            spec = make_stream(0, meta.nu, true, true, gw - kWarpsPerBlock, nwarps - kWarpsPerBlock, I, nq);
+            // (an abort shows in the next wait)
+            run_stream(gc, meta, spec, lane, a, pipe, true, tr ? tr + kTraceWarps + gw * 16 : nullptr);
         }
         __syncthreads();
         WISP_TRACE(1);
@@ -759,16 +863,18 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
             gc.t0 = 0;
             gc.t1 = t1;
             load_meta(a, 0, 0, nu, t1 * K, meta);
-            if (!gateup_units<MAXP>(gc, meta, u_lo, gw, nwarps, lane, a, pipe, done1)) goto done;
-            __syncthreads();
+            const Stream rest = make_stream(u_lo, nu, true, true, gw, nwarps, I, nq);
+            if (!run_stream(gc, meta, rest, lane, a, pipe, true, tr ? tr + kTraceWarps + gw * 16 + 8 : nullptr))
+                goto done;
             WISP_TRACE(2);
-            down_units<MAXQ>(gc, meta, gw, nwarps, lane, a, pipe, done1);
+            arrive_stream(gc, spec, nu, lane);
+            arrive_stream(gc, rest, nu, lane);
+            if (tr && lane == 0) tr[kTraceWarps + gw * 16 + 7] = globaltimer_ns();
             __syncthreads();
             WISP_TRACE(3);
         } else {
             // ---- several groups (or the generic variant): grid barriers between phases ---------
             if (!grid_barrier(a.bar, a.wait_ns)) goto done;
-            const int H = a.gc.H, I = a.gc.I;
             for (int g = 0; g < G; ++g) {
                 GroupCompute gc = a.gc;
                 const int t0 = __ldcg(pg.grp_start + g), t1 = __ldcg(pg.grp_start + g + 1);
@@ -779,7 +885,8 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
                 if (FAST) load_meta(a, g, p0, nu, (t1 - t0) * K, meta);
                 // phase 1: gate-up + SiLU-mul
                 if (FAST) {
-                    gateup_units<MAXP>(gc, meta, 0, gw, nwarps, lane, a, pipe, nullptr);
+                    run_stream(gc, meta, make_stream(0, nu, true, false, gw, nwarps, I, nq), lane, a, pipe,
+                               false);
                 } else {
                     gc.u_slot = pg.u_slot + p0;
                     gc.u_off = pg.u_off + p0 + g;
@@ -791,7 +898,8 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
                 if (!grid_barrier(a.bar, a.wait_ns)) goto done;
                 // phase 2: down x weight, last arrival per row quad combines
                 if (FAST) {
-                    down_units<MAXQ>(gc, meta, gw, nwarps, lane, a, pipe, nullptr);
+                    const Stream dn = make_stream(0, nu, false, true, gw, nwarps, I, nq);
+                    if (run_stream(gc, meta, dn, lane, a, pipe, false)) arrive_stream(gc, dn, nu, lane);
                 } else {
                     gc.u_slot = pg.u_slot + p0;
                     gc.u_off = pg.u_off + p0 + g;
@@ -809,8 +917,6 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
                         __threadfence_system();
                     }
                 }
-                (void)H;
-                (void)I;
             }
         }
     }
@@ -862,12 +968,13 @@ int launch_forward(const ForwardParams &p, int max_tokens_per_group, cudaStream_
                       p.gc.I <= kDqChunks * 256 && 2L * 2 * p.gc.H <= kStageBytes &&
                       4L * 2 * p.gc.I <= kStageBytes;
     if (fast) {
-        const size_t stages = (size_t)kWarpsPerBlock * kStages * kStageBytes;
+        // three stages per warp while the hidden states stay small enough for L1
+        // next to them, else two
+        ForwardParams q = p;
+        q.stages = (long)p.pg.T * p.gc.H * 2 <= 16384 ? 3 : 2;
+        const size_t stages = (size_t)kWarpsPerBlock * q.stages * kStageBytes;
         smem = smem > stages ? smem : stages;
-        if (max_tokens_per_group <= 1) return launch_t<1, true>(p, smem, stream);
-        if (max_tokens_per_group <= 2) return launch_t<2, true>(p, smem, stream);
-        if (max_tokens_per_group <= 4) return launch_t<4, true>(p, smem, stream);
-        return launch_t<8, true>(p, smem, stream);  // more pairs per expert: further passes
+        return launch_t<1, true>(q, smem, stream);
     }
     if (max_tokens_per_group <= 1) return launch_t<1, false>(p, smem, stream);
     if (max_tokens_per_group <= 4) return launch_t<4, false>(p, smem, stream);

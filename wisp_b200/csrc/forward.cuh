@@ -24,20 +24,22 @@ struct ForwardParams {
     // dataflow words (device, per layer, kFlowWords): see kFlow* below
     unsigned int *flow;
     int epoch;                      // launch parity: which set of counters this launch uses
+    int stages;                     // copy stages per warp (set by launch_forward)
+    // the other launch parity's activation buffer, reset here for the next launch
+    uint32_t *act_reset;
+    long act_reset_words;
     // optional %globaltimer trace (debug): [0..7] block 0 milestones, then 4 words per block
     unsigned long long *trace;
 };
 
 // Dataflow words: [kFlowPagerDone] sequence number of the call whose pager
 // outputs are complete; [kFlowSpecRead + e] blocks done reading the pre-call
-// expert map; [kFlowDone1 + e * kFlowMaxU + u] gate-up pairs finished for
-// unique expert u.  e is the launch parity; a launch zeroes the other set,
-// which the next launch uses.
-constexpr int kFlowMaxU = 256;
+// expert map.  e is the launch parity; a launch zeroes the other one, which
+// the next launch uses.  (Gate-up -> down ordering needs no words: a down
+// unit polls the activation rows themselves, see kActEmpty.)
 constexpr int kFlowPagerDone = 0;
 constexpr int kFlowSpecRead = 1;
-constexpr int kFlowDone1 = 8;
-constexpr int kFlowWords = kFlowDone1 + 2 * kFlowMaxU;
+constexpr int kFlowWords = 8;
 
 int launch_forward(const ForwardParams &p, int max_tokens_per_group, cudaStream_t stream);
 

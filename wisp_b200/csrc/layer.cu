@@ -103,6 +103,7 @@ struct wisp_layer {
     unsigned int *d_flow = nullptr;  // forward-kernel dataflow words (kFlowWords)
     int kparity = 0;                 // parity of the forward-kernel launches
     int64_t launches = 0;            // kernels this layer launched (all paths)
+    bool act_dirty = true;           // activation buffers not all kActEmpty (see forward_async)
     // per-call workspace, grown on demand
     int wsT = -1, wsK = 0;
     int32_t *d_slots = nullptr, *d_grp_start = nullptr, *d_grp_nu = nullptr, *d_grp_nhit = nullptr,
@@ -345,7 +346,9 @@ int ensure_ws(wisp_layer *L, int T, int K) {
     WISP_CUDA_TRY(cudaMalloc(&L->d_counters, sizeof(int32_t) * nblk));
     WISP_CUDA_TRY(cudaMemset(L->d_counters, 0, sizeof(int32_t) * nblk));
     if (L->H > 0 && L->I > 0) {
-        WISP_CUDA_TRY(cudaMalloc(&L->d_act, sizeof(__nv_bfloat16) * P * I));
+        // two halves, by launch parity (the one-launch forward polls its half)
+        WISP_CUDA_TRY(cudaMalloc(&L->d_act, sizeof(__nv_bfloat16) * 2 * P * I));
+        L->act_dirty = true;
         WISP_CUDA_TRY(cudaMalloc(&L->d_y, sizeof(__nv_bfloat16) * P * H));
     }
     const long words = (mailbox_words(nT, nK) + 31) & ~31L;
@@ -437,6 +440,7 @@ int reset_cold(wisp_layer *L) {
     const int nblk = (std::max(L->H, 8) + 3) / 4;
     WISP_CUDA_TRY(cudaMemset(L->d_counters, 0, sizeof(int32_t) * nblk));
     WISP_CUDA_TRY(cudaDeviceSynchronize());
+    L->act_dirty = true;
     return WISP_OK;
 }
 
@@ -456,6 +460,7 @@ int take_errors(wisp_layer *L) {
             cudaMemset(L->d_flow, 0, sizeof(unsigned int) * kFlowWords);
             cudaDeviceSynchronize();
         }
+        L->act_dirty = true;
         return fail(code, "wisp: an earlier forward routed an expert id outside [0, " +
                               std::to_string(L->E) + ")");
     }
@@ -547,6 +552,7 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
             rc = launch_decode_group(gc, nu[g], stream);
             if (rc) return rc;
             L->launches += kDecodeKernelsPerGroup;
+            L->act_dirty = true;
         }
         WISP_CUDA_TRY(cudaEventRecord(L->ev_group[g], stream));
     }
@@ -569,7 +575,16 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
     fp.gc.w13 = reinterpret_cast<const __nv_bfloat16 *>(L->d13);
     fp.gc.w2 = reinterpret_cast<const __nv_bfloat16 *>(L->d2);
     fp.gc.topk_w = w;
-    fp.gc.act = L->d_act;
+    // activation half of this launch's parity; the launch resets the other
+    // half to kActEmpty for the next one
+    const size_t act_half = (size_t)L->wsT * L->wsK * (size_t)std::max(L->I, 0);
+    if (L->act_dirty && act_half) {
+        WISP_CUDA_TRY(cudaMemsetAsync(L->d_act, 0xff, sizeof(__nv_bfloat16) * 2 * act_half, stream));
+        L->act_dirty = false;
+    }
+    fp.gc.act = L->d_act + (size_t)L->kparity * act_half;
+    fp.act_reset = reinterpret_cast<uint32_t *>(L->d_act + (size_t)(L->kparity ^ 1) * act_half);
+    fp.act_reset_words = (long)(act_half / 2);
     fp.gc.y = L->d_y;
     fp.gc.out = reinterpret_cast<__nv_bfloat16 *>(out);
     fp.gc.counters = L->d_counters;

@@ -83,7 +83,7 @@ __device__ __forceinline__ void gateup_rowpair(const GroupCompute &a, int u, int
                 if (lane == i) {
                     const float s = g / (1.0f + expf(-g));
                     const int p = a.u_pairs[qb + i];
-                    a.act[(size_t)p * I + j] = __float2bfloat16_rn(s * v);
+                    a.act[(size_t)p * I + j] = act_value(s * v);
                 }
             }
         }
