@@ -458,6 +458,13 @@ def main():
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if world > 1 or args.gpus > 1:
+        # every rank would pin the whole 58 GB expert stack: refuse before allocating
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "n_gpus": args.gpus, "unavailable":
+                              "multi-GPU run needs the expert-parallel path (not in this build)"}))
+        return
     line = run_wisp(args)
     if rank == 0:
         if args.gpus == 1 and args.cpu_sample_s > 0:
