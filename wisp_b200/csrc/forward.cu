@@ -109,6 +109,7 @@ __device__ bool wait_slot(const uint32_t *ready, int slot, uint32_t need, unsign
 // Per-block unique-expert lists of one group (shared memory).
 struct Meta {
     int nu, maxnp;
+    int total;  // speculation lists: unique experts of the call (resident or not)
     int slot[kMetaU], gen[kMetaU], off[kMetaU + 1];
     int pair[kMetaP], tok[kMetaP];
 };
@@ -122,7 +123,6 @@ constexpr int kMaxStages = 3;
 constexpr int kStageBytes = 8192;  // >= 2 rows x H (gate-up) and 4 rows x I (down), bf16
 constexpr int kPubLane = 31;       // lane that stores gate-up rows
 constexpr int kPairPass = 4;       // (token, k) pairs per pass over a unit's rows
-constexpr int kDownChunk = 4;      // consecutive down units per hand-out
 constexpr int kTraceWarps = 8 + 4 * 1024;  // per-warp records (16 words) start here in the trace buffer
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -206,45 +206,102 @@ __device__ __forceinline__ void pipe_issue(WarpPipe &w, int s, const void *src0,
     if (b1) bulk_g2s(dst + b0, src1, b1, w.bar + s);
 }
 
-// A warp's share of the units of experts [u0, u1) of the group's lists:
-// gate-up units first (unit k: expert u0 + k / I, row pair k % I; this warp
-// takes k = wid, wid + nw, ...), then down units (unit k: expert u0 + k / nq,
-// rows 4 (k % nq) ..; kDownChunk consecutive units per hand-out, hand-outs
-// round-robin starting with the warp after the one that took the last
-// gate-up unit).  A warp's stream is one pipeline: the copies of its first
-// down units are in flight while its last gate-up units compute.
+// A warp's share of the units of experts [u0, u1) of the group's lists: first
+// its gate-up units (unit k: expert u0 + k / I, row pair k % I; warp k % nw),
+// then its down units (unit d: expert u0 + d / nq, rows 4 (d % nq) ..), dealt
+// in chunks of kDownChunk consecutive units (mostly one expert, whose
+// activation rows then stay in registers) round-robin over the warps,
+// starting with the warp after the one that took the last gate-up unit, so
+// every warp gets nearly the same number of units.  A down unit comes after
+// every gate-up unit it reads in every warp's stream, so no wait can close a
+// cycle.  (Releasing an expert's down units right after its last gate-up
+// wave instead made warps that polled for rows still being computed hold up
+// their own gate-up units; the waves convoyed.)
+constexpr int kDownChunk = 4;
 struct Stream {
-    int u0;
-    int n_gu, my_gu;  // gate-up units: all / this warp's
-    int n_dn, my_dn;  // down units: all / this warp's
-    int dn_w;         // this warp's place in the down rotation
-    int wid, nw;
+    int u0, n_gu, n_dn, nch;  // first expert; gate-up units, down units, down chunks
+    int wid, nw, I, nq;
+    int nw_div, nw_mod;       // nw / I, nw % I
+    int my_gu, j0;            // this warp's gate-up units; its first down chunk
 };
 
 __device__ __forceinline__ Stream make_stream(int u0, int u1, bool gu, bool dn, int wid, int nw, int I,
                                               int nq) {
     Stream s;
+    const int ne = u1 > u0 ? u1 - u0 : 0;
     s.u0 = u0;
+    s.n_gu = gu ? ne * I : 0;
+    s.n_dn = dn ? ne * nq : 0;
+    s.nch = (s.n_dn + kDownChunk - 1) / kDownChunk;
     s.wid = wid;
     s.nw = nw;
-    const int ne = u1 > u0 ? u1 - u0 : 0;
-    s.n_gu = gu ? ne * I : 0;
+    s.I = I;
+    s.nq = nq;
+    s.nw_div = nw / I;
+    s.nw_mod = nw - s.nw_div * I;
     s.my_gu = wid < s.n_gu ? (s.n_gu - 1 - wid) / nw + 1 : 0;
-    s.n_dn = dn ? ne * nq : 0;
-    s.dn_w = (wid - s.n_gu % nw + nw) % nw;
-    const int nch = (s.n_dn + kDownChunk - 1) / kDownChunk;
-    int my = 0;
-    if (s.dn_w < nch) {
-        my = ((nch - 1 - s.dn_w) / nw + 1) * kDownChunk;
-        if ((nch - 1 - s.dn_w) % nw == 0) my -= nch * kDownChunk - s.n_dn;  // holds the short last hand-out
-    }
-    s.my_dn = my;
+    s.j0 = (wid - s.n_gu % nw + nw) % nw;
     return s;
 }
 
-// Down unit d (0-based among this warp's down units) -> unit index.
-__device__ __forceinline__ int down_unit(const Stream &s, int d) {
-    return (s.dn_w + (d / kDownChunk) * s.nw) * kDownChunk + d % kDownChunk;
+// Position in a warp's stream, advanced without divisions per item.
+struct Cursor {
+    int gu_left;  // gate-up items left, the current one included (0: in the down items)
+    int e, r;     // current item: expert (from u0), row pair or row quad
+    int j, d, d_end;
+    bool done;
+};
+
+__device__ __forceinline__ void cursor_chunk(Cursor &c, const Stream &S, int j) {
+    if (j >= S.nch) {
+        c.done = true;
+        return;
+    }
+    c.j = j;
+    c.d = j * kDownChunk;
+    c.d_end = min(c.d + kDownChunk, S.n_dn);
+    c.e = c.d / S.nq;
+    c.r = c.d - c.e * S.nq;
+}
+
+__device__ __forceinline__ Cursor cursor_begin(const Stream &S) {
+    Cursor c;
+    c.done = false;
+    c.gu_left = S.my_gu;
+    c.j = c.d = c.d_end = 0;
+    if (c.gu_left > 0) {
+        c.e = S.wid / S.I;
+        c.r = S.wid - c.e * S.I;
+    } else {
+        c.e = c.r = 0;
+        cursor_chunk(c, S, S.j0);
+    }
+    return c;
+}
+
+__device__ __forceinline__ void cursor_next(Cursor &c, const Stream &S) {
+    if (c.gu_left > 0) {
+        if (--c.gu_left > 0) {
+            c.e += S.nw_div;
+            c.r += S.nw_mod;
+            if (c.r >= S.I) {
+                c.r -= S.I;
+                ++c.e;
+            }
+        } else {
+            cursor_chunk(c, S, S.j0);
+        }
+        return;
+    }
+    if (c.done) return;
+    if (++c.d < c.d_end) {
+        if (++c.r == S.nq) {
+            c.r = 0;
+            ++c.e;
+        }
+    } else {
+        cursor_chunk(c, S, c.j + S.nw);
+    }
 }
 
 // One pass of a gate-up unit over P pairs starting at list entry qb.
@@ -297,7 +354,7 @@ struct ActCache {
 
 // One pass of a down unit over P pairs starting at list entry qb; `cache`
 // holds the pairs' activation rows when the expert has at most kPairPass pairs.
-template <int P, bool CACHED>
+template <int P, bool CACHED, int OFF = 0>
 __device__ __forceinline__ void dn_pass(const GroupCompute &a, const Meta &m, int qb, const unsigned char *st,
                                         int h0, int nr, int lane, const ActCache &cache) {
     const int H = a.H, I = a.I;
@@ -316,7 +373,7 @@ __device__ __forceinline__ void dn_pass(const GroupCompute &a, const Meta &m, in
             for (int r = 0; r < 4; ++r) wv[r] = ws[((r < nr ? r : 0) * I + c) >> 3];
 #pragma unroll
             for (int t = 0; t < P; ++t) {
-                const uint4 av = CACHED ? cache.v[t][c4] : ld_cg16(a.act + (size_t)m.pair[qb + t] * I + c);
+                const uint4 av = CACHED ? cache.v[OFF + t][c4] : ld_cg16(a.act + (size_t)m.pair[qb + t] * I + c);
 #pragma unroll
                 for (int r = 0; r < 4; ++r) acc[r][t] = dot8(wv[r], av, acc[r][t]);
             }
@@ -387,146 +444,141 @@ __device__ bool poll_act(const GroupCompute &a, const Meta &m, int q0, int np, i
 // expert's activation rows are complete (its W2 copy already in flight);
 // without it the caller separates the phases with a grid barrier.  Down units
 // store the weighted y; the row-quad arrivals are made later (arrive_stream).
-// Returns false when the kernel is aborting.
+// The gate-up items and the down items run in two tight loops (one compact
+// body each); the copy pipeline runs on across the change.  Returns false
+// when the kernel is aborting.
 // Optional per-warp trace (debug; `wtr` null when off): [0] start, [1] first
-// unit's data ready, [2] last gate-up unit's data ready, [3] all units done,
-// [4] ns in copy waits, [5] ns in activation polls, [6] units; %globaltimer.
+// unit's data ready, [2] gate-up items done, [3] all items done, [4] ns in
+// copy waits, [5] ns in activation polls, [6] items; %globaltimer.
 __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S, int lane,
                            const ForwardParams &fp, WarpPipe &w, bool dataflow,
                            unsigned long long *wtr = nullptr) {
     const int H = a.H, I = a.I;
-    const int nq = (H + 3) / 4;
     const uint32_t rowb = (uint32_t)H * 2;
-    const int total = S.my_gu + S.my_dn;
-    if (total == 0) return true;
     unsigned long long t_copy = 0, t_act = 0;
-    if (wtr && lane == 0) {
-        wtr[0] = globaltimer_ns();
-        wtr[6] = (unsigned long long)total;
-    }
-    // unit i of this warp -> expert u, and row pair j (gate-up) or row quad q (down)
-    auto describe = [&](int i, int &u, int &r) -> bool {
-        if (i < S.my_gu) {
-            const int k = S.wid + i * S.nw;
-            const int e = k / I;
-            u = S.u0 + e;
-            r = k - e * I;
-            return true;
-        }
-        const int k = down_unit(S, i - S.my_gu);
-        const int e = k / nq;
-        u = S.u0 + e;
-        r = k - e * nq;
-        return false;
-    };
-    auto issue = [&](int i, int s) -> bool {
-        int u, r;
-        const bool gu = describe(i, u, r);
+    int units = 0;
+    if (wtr && lane == 0) wtr[0] = globaltimer_ns();
+    // copy the weights of the item under cursor c into stage s
+    auto issue = [&](const Cursor &c, int s) -> bool {
+        const int u = S.u0 + c.e;
         if (m.gen[u] != 0) {  // expert paged in during this call: its slot must have landed
             int ok = 1;
             if (lane == 0) ok = wait_slot(fp.slot_ready, m.slot[u], (uint32_t)m.gen[u], fp.bar, fp.wait_ns);
             if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
         }
         if (lane == 0) {
-            if (gu) {
-                const __nv_bfloat16 *g = a.w13 + (size_t)m.slot[u] * (size_t)(2 * I) * H + (size_t)r * H;
+            if (c.gu_left > 0) {
+                const __nv_bfloat16 *g = a.w13 + (size_t)m.slot[u] * (size_t)(2 * I) * H + (size_t)c.r * H;
                 pipe_issue(w, s, g, rowb, g + (size_t)I * H, rowb);
             } else {
-                const int nr = min(4, H - 4 * r);
-                pipe_issue(w, s, a.w2 + (size_t)m.slot[u] * (size_t)H * I + (size_t)(4 * r) * I,
+                const int nr = min(4, H - 4 * c.r);
+                pipe_issue(w, s, a.w2 + (size_t)m.slot[u] * (size_t)H * I + (size_t)(4 * c.r) * I,
                            (uint32_t)nr * I * 2, nullptr, 0);
             }
         }
         w.pending |= 1u << s;
         return true;
     };
+    Cursor iss = cursor_begin(S), cmp = iss;
     bool ok = true;
-    for (int s = 0; s < w.nst && ok; ++s)
-        if (s < total) ok = issue(s, s);
+    for (int s0 = 0; s0 < w.nst && ok && !iss.done; ++s0) {
+        ok = issue(iss, s0);
+        cursor_next(iss, S);
+    }
+    auto wait_stage = [&](int s) -> bool {
+        const unsigned long long tw = wtr ? globaltimer_ns() : 0;
+        if (!pipe_wait(w, s, fp)) return false;
+        if (wtr) {
+            t_copy += globaltimer_ns() - tw;
+            if (units == 0 && lane == 0) wtr[1] = globaltimer_ns();
+        }
+        return true;
+    };
+    int s = 0;
+    // ---- gate-up items
+    while (ok && cmp.gu_left > 0) {
+        const int u = S.u0 + cmp.e, j = cmp.r;
+        const unsigned char *st = w.buf + s * kStageBytes;
+        if (!wait_stage(s)) {
+            ok = false;
+            break;
+        }
+        int qb = m.off[u];
+        const int q1 = m.off[u + 1];
+        for (; qb + 4 <= q1; qb += 4) gu_pass<4>(a, m, qb, st, j, lane);
+        if (qb + 2 <= q1) {
+            gu_pass<2>(a, m, qb, st, j, lane);
+            qb += 2;
+        }
+        if (qb < q1) gu_pass<1>(a, m, qb, st, j, lane);
+        __syncwarp();
+        ++units;
+        if (!iss.done) {
+            ok = issue(iss, s);
+            cursor_next(iss, S);
+        }
+        cursor_next(cmp, S);
+        s = (s + 1 == w.nst) ? 0 : s + 1;
+    }
+    if (wtr && lane == 0) wtr[2] = globaltimer_ns();
+    // ---- down items
     ActCache cache;
     int cache_u = -1, ready_u = -1;
-    int s = 0;
-    for (int i = 0; ok && i < total; ++i) {
-        int u, r;
-        const bool gu = describe(i, u, r);
+    while (ok && !cmp.done) {
+        const int u = S.u0 + cmp.e, h0 = 4 * cmp.r, nr = min(4, H - h0);
         const int q0 = m.off[u], q1 = m.off[u + 1], np = q1 - q0;
         const unsigned char *st = w.buf + s * kStageBytes;
-        if (gu) {
-            const unsigned long long tw = wtr ? globaltimer_ns() : 0;
-            if (!pipe_wait(w, s, fp)) {
+        const bool cached = np <= kPairPass;
+        if (dataflow && u != ready_u) {
+            const unsigned long long ta = wtr ? globaltimer_ns() : 0;
+            if (!(cached ? poll_act<true>(a, m, q0, np, lane, fp, cache)
+                         : poll_act<false>(a, m, q0, np, lane, fp, cache))) {
                 ok = false;
                 break;
             }
-            if (wtr) {
-                const unsigned long long now = globaltimer_ns();
-                t_copy += now - tw;
-                if (i == 0 && lane == 0) wtr[1] = now;
-                if (i + 1 == S.my_gu && lane == 0) wtr[2] = now;
-            }
-            int qb = q0;
-            for (; qb + kPairPass <= q1; qb += kPairPass) gu_pass<kPairPass>(a, m, qb, st, r, lane);
-            switch (q1 - qb) {
-                case 1: gu_pass<1>(a, m, qb, st, r, lane); break;
-                case 2: gu_pass<2>(a, m, qb, st, r, lane); break;
-                case 3: gu_pass<3>(a, m, qb, st, r, lane); break;
-                default: break;
+            if (wtr) t_act += globaltimer_ns() - ta;
+            ready_u = u;
+            if (cached) cache_u = u;
+        }
+        if (cached && u != cache_u) {  // this expert's activation rows, reused by its next units
+#pragma unroll
+            for (int t = 0; t < kPairPass; ++t)
+                if (t < np)
+#pragma unroll
+                    for (int c4 = 0; c4 < kDqChunks; ++c4) {
+                        const int c = c4 * 256 + lane * 8;
+                        if (c < I) cache.v[t][c4] = ld_cg16(a.act + (size_t)m.pair[q0 + t] * I + c);
+                    }
+            cache_u = u;
+        }
+        if (!wait_stage(s)) {
+            ok = false;
+            break;
+        }
+        if (cached) {
+            if (np == 4) {
+                dn_pass<4, true>(a, m, q0, st, h0, nr, lane, cache);
+            } else {
+                if (np >= 2) dn_pass<2, true>(a, m, q0, st, h0, nr, lane, cache);
+                if (np == 3) dn_pass<1, true, 2>(a, m, q0 + 2, st, h0, nr, lane, cache);
+                if (np == 1) dn_pass<1, true>(a, m, q0, st, h0, nr, lane, cache);
             }
         } else {
-            const bool cached = np <= kPairPass;
-            if (dataflow && u != ready_u) {
-                const unsigned long long ta = wtr ? globaltimer_ns() : 0;
-                if (!(cached ? poll_act<true>(a, m, q0, np, lane, fp, cache)
-                             : poll_act<false>(a, m, q0, np, lane, fp, cache))) {
-                    ok = false;
-                    break;
-                }
-                if (wtr) t_act += globaltimer_ns() - ta;
-                ready_u = u;
-                if (cached) cache_u = u;
+            int qb = q0;
+            for (; qb + 4 <= q1; qb += 4) dn_pass<4, false>(a, m, qb, st, h0, nr, lane, cache);
+            if (qb + 2 <= q1) {
+                dn_pass<2, false>(a, m, qb, st, h0, nr, lane, cache);
+                qb += 2;
             }
-            if (cached && u != cache_u) {  // this expert's activation rows, reused by its next units
-#pragma unroll
-                for (int t = 0; t < kPairPass; ++t)
-                    if (t < np)
-#pragma unroll
-                        for (int c4 = 0; c4 < kDqChunks; ++c4) {
-                            const int c = c4 * 256 + lane * 8;
-                            if (c < I) cache.v[t][c4] = ld_cg16(a.act + (size_t)m.pair[q0 + t] * I + c);
-                        }
-                cache_u = u;
-            }
-            const unsigned long long tw = wtr ? globaltimer_ns() : 0;
-            if (!pipe_wait(w, s, fp)) {
-                ok = false;
-                break;
-            }
-            if (wtr) {
-                t_copy += globaltimer_ns() - tw;
-                if (i == 0 && lane == 0) wtr[1] = globaltimer_ns();
-            }
-            const int h0 = 4 * r, nr = min(4, H - h0);
-            if (cached) {
-                switch (np) {
-                    case 1: dn_pass<1, true>(a, m, q0, st, h0, nr, lane, cache); break;
-                    case 2: dn_pass<2, true>(a, m, q0, st, h0, nr, lane, cache); break;
-                    case 3: dn_pass<3, true>(a, m, q0, st, h0, nr, lane, cache); break;
-                    case 4: dn_pass<4, true>(a, m, q0, st, h0, nr, lane, cache); break;
-                    default: break;
-                }
-            } else {
-                int qb = q0;
-                for (; qb + kPairPass <= q1; qb += kPairPass)
-                    dn_pass<kPairPass, false>(a, m, qb, st, h0, nr, lane, cache);
-                switch (q1 - qb) {
-                    case 1: dn_pass<1, false>(a, m, qb, st, h0, nr, lane, cache); break;
-                    case 2: dn_pass<2, false>(a, m, qb, st, h0, nr, lane, cache); break;
-                    case 3: dn_pass<3, false>(a, m, qb, st, h0, nr, lane, cache); break;
-                    default: break;
-                }
-            }
+            if (qb < q1) dn_pass<1, false>(a, m, qb, st, h0, nr, lane, cache);
         }
         __syncwarp();
-        if (i + w.nst < total) ok = issue(i + w.nst, s);
+        ++units;
+        if (!iss.done) {
+            ok = issue(iss, s);
+            cursor_next(iss, S);
+        }
+        cursor_next(cmp, S);
         s = (s + 1 == w.nst) ? 0 : s + 1;
     }
     if (!ok) {
@@ -537,6 +589,7 @@ __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S
         wtr[3] = globaltimer_ns();
         wtr[4] = t_copy;
         wtr[5] = t_act;
+        wtr[6] = (unsigned long long)units;
     }
     return true;
 }
@@ -545,15 +598,23 @@ __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S
 // then one lane per unit; the last of the nu arrivals on a quad sums the
 // group's tokens over k in routing order for its rows.
 __device__ void arrive_stream(const GroupCompute &a, const Stream &S, int nu, int lane) {
-    if (S.my_dn == 0) return;
-    const int nq = (a.H + 3) / 4;
+    if (S.n_dn == 0 || S.j0 >= S.nch) return;
     __threadfence();
     __syncwarp();
-    for (int db = 0; db < S.my_dn; db += 32) {
-        const int d = db + lane;
+    // this warp's down units, 32 at a time (lane l takes the l-th)
+    int j = S.j0, d = j * kDownChunk;
+    while (j < S.nch) {
+        int mine = -1;
+        for (int l = 0; l < 32 && j < S.nch; ++l) {
+            if (l == lane) mine = d;
+            if (++d >= min((j + 1) * kDownChunk, S.n_dn)) {
+                j += S.nw;
+                d = j * kDownChunk;
+            }
+        }
         int last = 0, q = 0;
-        if (d < S.my_dn) {
-            q = down_unit(S, d) % nq;
+        if (mine >= 0) {
+            q = mine % S.nq;
             last = (atomicAdd(&a.counters[q], 1) == nu - 1);
         }
         unsigned todo = __ballot_sync(0xffffffffu, last);
@@ -671,6 +732,7 @@ __device__ bool build_spec_meta(const ForwardParams &fp, Meta &m, int *pos) {
         const int nres = __shfl_sync(0xffffffffu, incl, 31);
         if (lane == 0) {
             m.nu = nres;
+            m.total = total;
             if (total > pg.cap) s_flag = 1;
         }
     }
@@ -838,6 +900,20 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
             spec = make_stream(0, meta.nu, true, true, gw - kWarpsPerBlock, nwarps - kWarpsPerBlock, I, nq);
             // (an abort shows in the next wait)
             run_stream(gc, meta, spec, lane, a, pipe, true, tr ? tr + kTraceWarps + gw * 16 : nullptr);
+        }
+        // every expert of the call was resident before it: the pager will find
+        // one group of hits only, so nothing is left but the speculative
+        // stream's row-quad arrivals; the warps of this block make them and
+        // leave without waiting for the pager or for each other (the condition
+        // is the same for every warp of the block)
+        if (spec_here && meta.total == meta.nu) {
+            GroupCompute gc = a.gc;
+            gc.t0 = 0;
+            gc.t1 = pg.T;
+            arrive_stream(gc, spec, meta.nu, lane);
+            if (tr && lane == 0) tr[kTraceWarps + gw * 16 + 7] = globaltimer_ns();
+            WISP_TRACE(3);
+            goto done;
         }
         __syncthreads();
         WISP_TRACE(1);
