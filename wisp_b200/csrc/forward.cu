@@ -135,11 +135,20 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+// Weight rows are read once per forward: their L2 lines go first, so the
+// stream does not push the kernel's code and the small shared inputs (hidden
+// states, activations, y) out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t pol) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() {
@@ -162,6 +171,7 @@ struct WarpPipe {
     uint32_t phase;      // bit s: parity to wait for on stage s
     uint32_t pending;    // bit s: a copy into stage s has not been waited for
     int nst;             // stages in use
+    uint64_t pol;        // L2 policy of the weight copies
 };
 
 // Wait for stage s (bounded); on timeout record it and abort.
@@ -202,8 +212,8 @@ __device__ __forceinline__ void pipe_issue(WarpPipe &w, int s, const void *src0,
     unsigned char *dst = w.buf + s * kStageBytes;
     fence_proxy_async();
     mbar_expect_tx(w.bar + s, b0 + b1);
-    bulk_g2s(dst, src0, b0, w.bar + s);
-    if (b1) bulk_g2s(dst + b0, src1, b1, w.bar + s);
+    bulk_g2s(dst, src0, b0, w.bar + s, w.pol);
+    if (b1) bulk_g2s(dst + b0, src1, b1, w.bar + s, w.pol);
 }
 
 // A warp's share of the units of experts [u0, u1) of the group's lists: first
@@ -675,7 +685,8 @@ __device__ __forceinline__ void down_generic(const GroupCompute &gc, int nu, int
 // Block-local lists of the experts resident before the call (speculative
 // phase 1).  Returns false when speculation does not apply (more experts than
 // the cap: several groups; or ids out of range: the pager reports them).
-// `pos` is scratch for E ints.
+// `pos` is scratch for 2 E ints (the second half holds a copy of the expert
+// map, loaded together with the routing ids: one global round trip).
 __device__ bool build_spec_meta(const ForwardParams &fp, Meta &m, int *pos) {
     __shared__ uint32_t s_mask[32];
     __shared__ int s_flag;
@@ -683,8 +694,10 @@ __device__ bool build_spec_meta(const ForwardParams &fp, Meta &m, int *pos) {
     const PagerParams &pg = fp.pg;
     const int P = pg.T * pg.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (P > kSpecMaxPairs || pg.E > 1024) return false;
+    int *s_emap = pos + pg.E;
     if (tid < 32) s_mask[tid] = 0;
     if (tid == 0) s_flag = 0;
+    for (int e = tid; e < pg.E; e += blockDim.x) s_emap[e] = pg.emap[e];
     __syncthreads();
     for (int p = tid; p < P; p += blockDim.x) {
         const long long e = load_id64(pg.ids, pg.ids64, p);
@@ -705,7 +718,7 @@ __device__ bool build_spec_meta(const ForwardParams &fp, Meta &m, int *pos) {
         for (uint32_t v = w; v;) {
             const int b = __ffs(v) - 1;
             v &= v - 1;
-            if (pg.emap[lane * 32 + b] >= 0) keep |= 1u << b;
+            if (s_emap[lane * 32 + b] >= 0) keep |= 1u << b;
         }
         const int c = __popc(keep);
         int incl = c;
@@ -719,7 +732,7 @@ __device__ bool build_spec_meta(const ForwardParams &fp, Meta &m, int *pos) {
             const int b = __ffs(v) - 1;
             v &= v - 1;
             const int e = lane * 32 + b;
-            m.slot[idx] = pg.emap[e];
+            m.slot[idx] = s_emap[e];
             m.gen[idx] = 0;
             pos[e] = idx;
             ++idx;
@@ -860,6 +873,7 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
         pipe.nst = a.stages;
         pipe.buf = smem + (size_t)warp * a.stages * kStageBytes;
         pipe.bar = s_bars[warp];
+        pipe.pol = l2_evict_first_policy();
         if (lane == 0) {
             for (int st = 0; st < a.stages; ++st) mbar_init(pipe.bar + st, 1);
             fence_proxy_async();
@@ -1039,7 +1053,7 @@ int launch_t(const ForwardParams &p, size_t smem, cudaStream_t stream) {
 
 int launch_forward(const ForwardParams &p, int max_tokens_per_group, cudaStream_t stream) {
     size_t smem = pager_smem_bytes(p.pg.E, p.pg.cap, p.pg.T, p.pg.K);
-    smem = smem > sizeof(int) * 1024 ? smem : sizeof(int) * 1024;  // speculation's expert index
+    smem = smem > sizeof(int) * 2048 ? smem : sizeof(int) * 2048;  // speculation's expert index + map
     const bool fast = (long)p.pg.T * p.pg.K <= kMetaP && p.gc.H <= kGuChunks * 256 &&
                       p.gc.I <= kDqChunks * 256 && 2L * 2 * p.gc.H <= kStageBytes &&
                       4L * 2 * p.gc.I <= kStageBytes;
