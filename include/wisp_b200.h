@@ -183,6 +183,37 @@ WISP_API int wisp_expert_compute_noalloc(int32_t device, const void *x, const vo
                                          int32_t num_tokens, int32_t top_k, int32_t hidden,
                                          int32_t inter, void *out, void *stream);
 
+/*
+ * Expert parallelism (no counterpart in the reference, which runs one GPU per
+ * layer).  Rank r of `world` owns experts [r * experts_per_rank,
+ * (r + 1) * experts_per_rank) and pages only those; the (token, k) pairs go
+ * to their owners by NCCL all-to-all, each owner runs wisp_moe_forward on the
+ * rows it received (top_k 1, local expert ids), and the weighted rows come
+ * back for the combine.
+ *
+ * wisp_ep_dispatch: from x [T][H] bf16, topk_ids [T][k] (int32, or int64 when
+ * ids_int64), topk_weights [T][k] fp32, writes the send buffers in owner
+ * order (pairs of one owner keep their (t, k) order): send_x [T*k][H] bf16,
+ * send_meta [T*k][2] int32 = (local expert id, weight bits), send_counts
+ * [world + 1] int64 = rows per owner, then the number of ids outside
+ * [0, world * experts_per_rank) (non-zero: nothing else is valid), and
+ * pair_pos [T*k] int32 = the send row of pair t*k+j.  Asynchronous on
+ * `stream`; hidden a multiple of 8, world <= 64.
+ */
+WISP_API int wisp_ep_dispatch(const void *x, const void *topk_ids, int32_t ids_int64,
+                              const float *topk_weights, int32_t num_tokens, int32_t top_k,
+                              int32_t hidden, int32_t experts_per_rank, int32_t world, void *send_x,
+                              int32_t *send_meta, int64_t *send_counts, int32_t *pair_pos,
+                              void *stream);
+
+/*
+ * wisp_ep_combine: out[t] = sum over j in routing order of y_back[pair_pos[t*k+j]]
+ * (fp32, stored bf16) -- the routing-order sum of the one-GPU forward, so the
+ * result is byte-identical to it.  y_back [T*k][H] bf16 in send order.
+ */
+WISP_API int wisp_ep_combine(const void *y_back, const int32_t *pair_pos, int32_t num_tokens,
+                             int32_t top_k, int32_t hidden, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,9 @@ SIGNATURES = {
     "wisp_layer_config": (ctypes.c_int, [_vp, _c_int32, _c_int64]),
     "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,
                                                    _c_int32, _c_int32, _c_int32, _c_int32, _vp, _vp]),
+    "wisp_ep_dispatch": (ctypes.c_int, [_vp, _vp, _c_int32, _vp, _c_int32, _c_int32, _c_int32, _c_int32,
+                                        _c_int32, _vp, _vp, _vp, _vp, _vp]),
+    "wisp_ep_combine": (ctypes.c_int, [_vp, _vp, _c_int32, _c_int32, _c_int32, _vp, _vp]),
 }
 
 

@@ -327,9 +327,17 @@ void free_ws(wisp_layer *L) {
     L->wsK = 0;
 }
 
+// Grow the per-call workspace (geometrically, so a varying batch settles).
+// Frees and allocations wait for the whole device first: cudaFree and
+// cudaFreeHost synchronise implicitly and stall the page-in thread's copy
+// calls meanwhile, so one issued while another layer's forward kernel waits
+// for its page-ins would hold that kernel until its wait limit runs out.
+// cudaDeviceSynchronize waits without stalling the page-in thread.
 int ensure_ws(wisp_layer *L, int T, int K) {
     if (T <= L->wsT && K <= L->wsK) return WISP_OK;
-    int nT = std::max(T, std::max(L->wsT, 16)), nK = std::max(K, std::max(L->wsK, 8));
+    const int nT = std::max({T, L->wsT > 0 ? 2 * L->wsT : 0, 16});
+    const int nK = std::max({K, L->wsK, 8});
+    WISP_CUDA_TRY(cudaDeviceSynchronize());
     free_ws(L);
     const size_t P = std::max<size_t>((size_t)nT * nK, 1);
     WISP_CUDA_TRY(cudaMalloc(&L->d_slots, sizeof(int32_t) * P));
@@ -663,6 +671,9 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     if (device < 0 || device >= 64) return fail(WISP_ERR_INVALID, "wisp_layer_create: bad device");
     DeviceGuard guard(device);
     std::call_once(g_write32_once, init_write32);
+    // other layers' forwards may be in flight: let them finish before the
+    // allocations below (see ensure_ws)
+    WISP_CUDA_TRY(cudaDeviceSynchronize());
     cudaPointerAttributes pa{};
     for (const void *hp : {host_w13, host_w2}) {
         if (cudaPointerGetAttributes(&pa, hp) != cudaSuccess || pa.type != cudaMemoryTypeHost) {
