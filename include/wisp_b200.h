@@ -145,7 +145,11 @@ WISP_API int wisp_layer_sync(wisp_layer *layer);
 
 /*
  * Tunables: WISP_CFG_ASYNC (1: single-launch forward with asynchronous
- * page-in, the default; 0: host-synchronous path), WISP_CFG_WAIT_NS (limit of
+ * page-in, the default of resident layers; 0: host-synchronous path, the
+ * default of paged layers -- a paged single-launch forward waits inside the
+ * kernel for copies a host thread issues after the launch, so the caller must
+ * queue no other device work while it pages in, or the copies can be held
+ * behind that work until the wait limit), WISP_CFG_WAIT_NS (limit of
  * one device-side wait, default 10 s), WISP_CFG_DROP_PAGEINS (test fault: the
  * host silently skips the next n page-ins of this layer),
  * WISP_CFG_TRACE_BUFFER (debug: device address of a uint64 buffer of

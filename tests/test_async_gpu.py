@@ -119,3 +119,51 @@ def test_dropped_pagein_times_out_without_fault_and_layer_recovers():
     assert c["max_abs"] <= 1e-2 and c["mean_rel"] <= 1e-3, c
     torch.cuda.synchronize()
     st.close()
+
+
+def test_workspace_growth_while_another_layer_pages_in():
+    """A forward that grows its workspace (more rows than any earlier call)
+    right after another layer's forward that is still waiting for page-ins:
+    the reallocation waits for the device first, so it does not stall the
+    page-in thread (that forward would otherwise wait until its limit and
+    restart cold)."""
+    E, H, I, K = 16, 512, 256, 1
+    w13, w2, g = _weights(E, H, I, 21)
+    a, b = _state(w13, w2, 3, True), _state(w13, w2, 3, True)
+    for st in (a, b):
+        st.configure(wait_ns=2_000_000_000)
+    from wisp_b200.integrations.vllm.fused_moe import WispMoEState
+    full = WispMoEState(w13, w2, E, "resident", DEV, 0)
+    full.prime_identity()
+    for T in (8, 40, 90):
+        xa, xb = (torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV) for _ in range(2))
+        ia, ib = (torch.randint(0, E, (T, K), generator=g).to(torch.int32).to(DEV) for _ in range(2))
+        wa, wb = (torch.rand(T, K, generator=g).to(DEV) for _ in range(2))
+        oa = a.forward(xa, wa, ia)   # pages in, waits on the page-in thread
+        ob = b.forward(xb, wb, ib)   # grows b's workspace meanwhile
+        a.synchronize()
+        b.synchronize()
+        assert torch.equal(oa, full.forward(xa, wa, ia)), T
+        assert torch.equal(ob, full.forward(xb, wb, ib)), T
+    for st in (a, b, full):
+        st.close()
+
+
+def test_paged_layers_default_to_the_synchronous_path():
+    from wisp_b200.integrations.vllm.fused_moe import WispMoEState
+    E, H, I, K = 16, 256, 128, 4
+    w13, w2, g = _weights(E, H, I, 22)
+    paged = WispMoEState(w13, w2, 6, "paged", DEV, 0)
+    res = WispMoEState(w13, w2, E, "resident", DEV, 0)
+    res.prime_identity()
+    x = torch.randn(5, H, generator=g).to(torch.bfloat16).to(DEV)
+    w, ids = wl.softmax_topk(torch.randn(5, E, generator=g), K)
+    out = paged.forward(x, w.to(DEV), ids.to(DEV))
+    paged.synchronize()
+    # synchronous path: pager kernel + two kernels per group; resident: one launch
+    res.forward(x, w.to(DEV), ids.to(DEV))
+    assert paged.telemetry()["kernel_launches"] == 1 + 2 * paged.telemetry()["groups"]
+    assert res.telemetry()["kernel_launches"] == 1
+    assert torch.equal(out, res.forward(x, w.to(DEV), ids.to(DEV)))
+    paged.close()
+    res.close()

@@ -6,8 +6,9 @@
 // a copy-engine stream for page-in from the caller's pinned host masters,
 // and the compute kernels.
 //
-// Forward, asynchronous path (default when top_k <= cap, i.e. when the
-// working-set overflow of fused_moe.py:313-327 cannot happen):
+// Forward, one-launch path (default for resident layers; a paged layer opts
+// in with WISP_CFG_ASYNC, when top_k <= cap so the working-set overflow of
+// fused_moe.py:313-327 cannot happen):
 //   * one cooperative launch of the persistent forward kernel (forward.cu)
 //     on the caller's stream: pager, then per group gate-up / down / combine;
 //     the host does not wait;
@@ -17,10 +18,12 @@
 //     published that the last earlier group reading the victim slot is done,
 //     issues the two H2D copies on the layer's copy stream followed by a
 //     stream memory write of the slot's generation flag, which is what the
-//     kernel waits on before reading the slot.
-// Forward, synchronous path (top_k > cap, or WISP_CFG_ASYNC = 0): the pager
-// kernel runs alone, the host reads the mailbox, issues the page-ins of each
-// group with event ordering and launches the per-group decode kernels.
+//     kernel waits on before reading the slot.  (The kernel waits on work
+//     issued after it; see wisp_layer_create for why paged layers do not
+//     take this path by default.)
+// Forward, synchronous path (default for paged layers; top_k > cap): the
+// pager kernel runs alone, the host reads the mailbox, issues the page-ins of
+// each group with event ordering and launches the per-group decode kernels.
 // Both paths run the same warp arithmetic (moe_body.cuh), so their outputs are
 // byte-identical.
 #include <cuda.h>
@@ -724,6 +727,14 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     if (rc) return bail(rc);
     if (cudaDeviceSynchronize() != cudaSuccess)
         return bail(fail(WISP_ERR_CUDA, "wisp_layer_create: device sync failed"));
+    // One-launch forward by default only where it never waits on page-ins:
+    // a paged forward's kernel would wait for copies a host thread issues
+    // after the launch on another stream, and CUDA may queue those copies in a
+    // hardware queue behind work the caller has already queued after the
+    // kernel -- the kernel then waits until its limit.  WISP_CFG_ASYNC = 1
+    // opts a paged layer in where the caller queues nothing on the device
+    // while its forwards page in.
+    L->async = (mode == WISP_MODE_RESIDENT);
     const char *env = getenv("WISP_B200_SYNC");
     if (env && env[0] == '1') L->async = false;
     *out = L;

@@ -301,7 +301,13 @@ class WispMoEState:
 
     def configure(self, *, asynchronous: bool | None = None, wait_ns: int | None = None,
                   drop_pageins: int | None = None) -> None:
-        """Runtime knobs of the native layer (see ``wisp_layer_config``)."""
+        """Runtime knobs of the native layer (see ``wisp_layer_config``).
+
+        ``asynchronous``: the single-launch forward (default for resident
+        layers).  A paged layer defaults to the host-synchronous forward: a
+        paged single-launch forward waits inside its kernel for page-in copies
+        a host thread issues after the launch, so it suits only callers that
+        queue no other device work while it pages in."""
         L = _lib.lib()
         for key, val in ((_lib.CFG_ASYNC, asynchronous), (_lib.CFG_WAIT_NS, wait_ns),
                          (_lib.CFG_DROP_PAGEINS, drop_pageins)):
