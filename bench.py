@@ -377,6 +377,147 @@ def resident_phase(args, masters, dev, hbm_peak, batch):
             "frac": gbs / hbm_peak}
 
 
+def make_shard_masters(layers, dev, rank, world):
+    """Pinned bf16 host masters of this rank's experts per layer: the same
+    N(0, 0.02) weights as make_masters (same per-layer seeds), sliced to the
+    shard, so the whole model is identical at every rank count."""
+    E = SHAPE.experts
+    lo, hi = rank * E // world, (rank + 1) * E // world
+    out = []
+    for layer in range(layers):
+        g = torch.Generator(device=dev).manual_seed(1000 + layer)
+        t = torch.randn(E, 2 * SHAPE.inter, SHAPE.hidden, device=dev, generator=g, dtype=torch.float32)
+        h13 = t[lo:hi].mul_(0.02).to(torch.bfloat16).cpu().pin_memory()
+        del t
+        t = torch.randn(E, SHAPE.hidden, SHAPE.inter, device=dev, generator=g, dtype=torch.float32)
+        h2 = t[lo:hi].mul_(0.02).to(torch.bfloat16).cpu().pin_memory()
+        del t
+        out.append((h13, h2))
+    torch.cuda.synchronize()
+    return out
+
+
+def run_wisp_ep(args):
+    """Expert-parallel stack over the torchrun ranks (one GPU each): rank r owns
+    experts [r E/P, (r+1) E/P) of every layer in its own pinned memory and
+    pages them into cap = min(--cap, E/P) slots per layer; each rank decodes its
+    own batch of --batch tokens (weak scaling: global batch = P x batch),
+    tokens exchanged by NCCL all-to-all.  Times are CUDA events, max over ranks."""
+    import datetime
+
+    import torch.distributed as dist
+    from wisp_b200.expert_parallel import EPMoELayer
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    L, B = args.layers, args.batch
+    E = SHAPE.experts
+    per = E // world
+    C = min(args.cap, per)
+    total = args.warmup + args.steps
+    t0 = time.time()
+    masters = make_shard_masters(L, dev, rank, world)
+    layers = [EPMoELayer(h13, h2, E, C, "paged", dev, i) for i, (h13, h2) in enumerate(masters)]
+    ids_all, w_all = routing(total, L, B * world)
+    ids_d = torch.from_numpy(np.ascontiguousarray(ids_all[:, :, rank * B:(rank + 1) * B])).to(dev)
+    w_d = torch.from_numpy(np.ascontiguousarray(w_all[:, :, rank * B:(rank + 1) * B])).to(dev)
+    x_d = wl.hidden_states(B * world, SHAPE.hidden, seed=0)[rank * B:(rank + 1) * B].contiguous().to(dev)
+    out_d = torch.empty_like(x_d)
+    setup_s = time.time() - t0
+
+    def step(s, x, w, ids, out):
+        for layer in range(L):
+            layers[layer].forward(x, w[s, layer], ids[s, layer], out=out)
+
+    for s in range(args.warmup):
+        step(s, x_d, w_d, ids_d, out_d)
+    torch.cuda.synchronize()
+    for lay in layers:
+        lay.local.synchronize()
+    tel0 = [lay.local.telemetry() for lay in layers]
+    dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(dev.index)
+    with clk:
+        torch.cuda.synchronize()
+        ev0.record()
+        for s in range(args.warmup, total):
+            step(s, x_d, w_d, ids_d, out_d)
+        ev1.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    for lay in layers:
+        lay.local.synchronize()
+    tel1 = [lay.local.telemetry() for lay in layers]
+
+    def delta(key):
+        return sum(b[key] - a[key] for a, b in zip(tel0, tel1))
+
+    # per forward: route + pack + combine kernels of the exchange, plus the shard's own launches
+    stats = torch.tensor([ev0.elapsed_time(ev1), float(delta("pagein_bytes")),
+                          float(delta("kernel_launches") + 3 * L * args.steps),
+                          float(delta("unique_experts"))], dtype=torch.float64, device=dev)
+    mx = stats.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    dist.all_reduce(stats, op=dist.ReduceOp.SUM)
+    ms = float(mx[0])
+
+    # end to end: this rank's routing + hidden states in from pinned host, output back, every step
+    ids_h = torch.from_numpy(np.ascontiguousarray(ids_all[:, :, rank * B:(rank + 1) * B])).pin_memory()
+    w_h = torch.from_numpy(np.ascontiguousarray(w_all[:, :, rank * B:(rank + 1) * B])).pin_memory()
+    x_h = x_d.cpu().pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+    ids_s = torch.empty((L, B, SHAPE.top_k), dtype=ids_d.dtype, device=dev)
+    w_s = torch.empty((L, B, SHAPE.top_k), dtype=w_d.dtype, device=dev)
+    e2e_steps = min(args.steps, 8)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record()
+    for j in range(e2e_steps):
+        s = args.warmup + (j % args.steps)
+        ids_s.copy_(ids_h[s], non_blocking=True)
+        w_s.copy_(w_h[s], non_blocking=True)
+        x_d.copy_(x_h, non_blocking=True)
+        for layer in range(L):
+            layers[layer].forward(x_d, w_s[layer], ids_s[layer], out=out_d)
+        out_h.copy_(out_d, non_blocking=True)
+    ev3.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([ev2.elapsed_time(ev3)], dtype=torch.float64, device=dev)
+    dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    for lay in layers:
+        lay.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    h2d = h2d_peak_gbs(dev) if rank == 0 else 0.0
+    pagein_gbs = float(stats[1]) / (ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": world * B * args.steps / (ms * 1e-3), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded Zipf routing trace; random-init N(0,0.02) weights)",
+        "config": {"workload": f"qwen3-30b-a3b {L}-layer expert stack, expert-parallel over {world} GPUs, "
+                               f"decode batch {B} per GPU, cap {C} per GPU",
+                   "layers": L, "batch_per_gpu": B, "global_batch": B * world, "cap_per_gpu": C,
+                   "experts_per_gpu": per, "parallelism": f"ep{world}", "routing": "zipf1.1 reuse0.6",
+                   "l2": "inputs larger than L2 (each step reads every layer's routed experts from HBM)"},
+        "gpu_launches": int(stats[2]),
+        "roofline": None,
+        "pagein": {"gbs_all_ranks": pagein_gbs, "h2d_peak_gbs_per_gpu": h2d,
+                   "frac_of_per_gpu_peak_x_gpus": pagein_gbs / (h2d * world) if h2d else None,
+                   "bytes": float(stats[1])},
+        "e2e": {"value": world * B * e2e_steps / (float(e2e_ms[0]) * 1e-3), "unit": "tok/s",
+                "h2d_bytes_per_step": int(ids_s.numel() * ids_s.element_size() + w_s.numel()
+                                          * w_s.element_size() + x_h.numel() * x_h.element_size()) * world,
+                "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()) * world,
+                "steps": e2e_steps},
+        "clocks": clk.summary(),
+        "setup_s": setup_s,
+    }
+
+
 def run_reference(args):
     """CPU restatement of the reference path on the host cores (bounded sample)."""
     from oracle.moe import moe_reference  # noqa: F401
@@ -459,11 +600,10 @@ def main():
         print(json.dumps(line))
         return
     world = int(os.environ.get("WORLD_SIZE", 1))
-    if world > 1 or args.gpus > 1:
-        # every rank would pin the whole 58 GB expert stack: refuse before allocating
+    if world > 1:
+        line = run_wisp_ep(args)
         if rank == 0:
-            print(json.dumps({"metric": METRIC, "n_gpus": args.gpus, "unavailable":
-                              "multi-GPU run needs the expert-parallel path (not in this build)"}))
+            print(json.dumps(line))
         return
     line = run_wisp(args)
     if rank == 0:
