@@ -1,0 +1,281 @@
+// Prefill expert compute for one token group on tcgen05 tensor cores; see
+// gemm_sm100.cuh for the data flow and the kernel structure.
+#include "gemm_sm100.cuh"
+#include "prefill.cuh"
+
+#include <mutex>
+
+namespace wisp {
+namespace gemm {
+namespace {
+
+__device__ __forceinline__ unsigned char *align1024(unsigned char *p) {
+    const uint32_t a = s_addr(p);
+    return p + ((1024u - (a & 1023u)) & 1023u);
+}
+
+// X_perm[q] = x[token of pair q]: one warp per row, 16-byte copies.
+__global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int K, int H8, uint4 *xp) {
+    const int q = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (q >= P) return;
+    const uint4 *src = x + (size_t)(u_pairs[q] / K) * H8;
+    uint4 *dst = xp + (size_t)q * H8;
+    for (int c = threadIdx.x & 31; c < H8; c += 32) dst[c] = src[c];
+}
+
+// Setup common to both GEMMs: tile lookup, barriers, TMEM.  Returns false when
+// this CTA has no tile.
+__device__ __forceinline__ bool tile_setup(const GroupGemm &g, Ring &R, int &u, int &q0, int &rows) {
+    __shared__ int s_u, s_q0, s_rows;
+    if (threadIdx.x == 0) {
+        int uu = -1, qq = 0, rr = 0;
+        if (!find_mtile(g, blockIdx.x, uu, qq, rr)) uu = -1;
+        s_u = uu;
+        s_q0 = qq;
+        s_rows = rr;
+        R.abort = 0;
+        R.issued = R.consumed = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&R.full[s], 1);
+            mbar_init(&R.empty[s], 1);
+        }
+        mbar_init(&R.tmem_full, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+    u = s_u;
+    q0 = s_q0;
+    rows = s_rows;
+    if (u < 0) return false;
+    if ((threadIdx.x >> 5) == 0) tmem_alloc(&R.tmem_base, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    return true;
+}
+
+__device__ __forceinline__ void tile_teardown(Ring &R, const GroupGemm &g) {
+    tc_fence_before();
+    __syncthreads();
+    if (R.abort) drain_ring(R, g);
+    __syncthreads();
+    tc_fence_after();
+    if ((threadIdx.x >> 5) == 0) tmem_dealloc(R.tmem_base, kTmemCols);
+}
+
+// Epilogue wait for the accumulator (all threads); false after an abort.  The
+// result is uniform over the warp and the warp leaves converged, as the
+// .sync.aligned TMEM loads that follow require (lanes 0 of warps 0 and 1 come
+// from the producer and MMA loops).
+__device__ __forceinline__ bool wait_accumulator(Ring &R, const GroupGemm &g) {
+    volatile int *abort = &R.abort;
+    const bool ok = mbar_wait(&R.tmem_full, 0, g.wait_ns, abort) && !*abort;
+    const bool all = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    return all;
+}
+
+// Gate-up + SiLU-mul: grid (m tiles, I / 128).
+__global__ void __launch_bounds__(kThreads, 1)
+    gateup_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w13,
+                       GroupGemm g) {
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ Ring R;
+    unsigned char *stages = align1024(smem_raw);
+    int u, q0, rows;
+    if (!tile_setup(g, R, u, q0, rows)) return;
+    const int I = g.I, j0 = blockIdx.y * kHalfN;
+    const int slot_row = g.u_slot[u] * 2 * I;
+    const int kb_count = g.H / kBK;
+    mainloop(&map_x, &map_w13, q0, slot_row + j0, slot_row + I + j0, kb_count, stages, R, g);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = warp * 32 + lane;
+    if (wait_accumulator(R, g)) {
+        const uint32_t tbase = R.tmem_base + ((uint32_t)(warp * 32) << 16);
+        __nv_bfloat16 *dst = g.act_perm + (size_t)(q0 + row) * I + j0;
+        for (int c0 = 0; c0 < kHalfN; c0 += 32) {
+            uint32_t gr[32], ur[32];
+            tmem_ld32(tbase + c0, gr);
+            tmem_ld32(tbase + kHalfN + c0, ur);
+            if (row < rows) {
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    float o[2];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const float gv = round_bf16(__uint_as_float(gr[i + h]));
+                        const float uv = round_bf16(__uint_as_float(ur[i + h]));
+                        o[h] = gv / (1.0f + expf(-gv)) * uv;
+                    }
+                    packed[i / 2] = (uint32_t)__bfloat16_as_ushort(act_value(o[0])) |
+                                    ((uint32_t)__bfloat16_as_ushort(act_value(o[1])) << 16);
+                }
+                uint4 *d4 = reinterpret_cast<uint4 *>(dst + c0);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            }
+        }
+    }
+    tile_teardown(R, g);
+}
+
+// Down x routing weight: grid (m tiles, H / 256).
+__global__ void __launch_bounds__(kThreads, 1)
+    down_gemm_kernel(const __grid_constant__ CUtensorMap map_act, const __grid_constant__ CUtensorMap map_w2,
+                     GroupGemm g) {
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ Ring R;
+    unsigned char *stages = align1024(smem_raw);
+    int u, q0, rows;
+    if (!tile_setup(g, R, u, q0, rows)) return;
+    const int H = g.H, n0 = blockIdx.y * kBN;
+    const int slot_row = g.u_slot[u] * H;
+    const int kb_count = g.I / kBK;
+    mainloop(&map_act, &map_w2, q0, slot_row + n0, slot_row + n0 + kHalfN, kb_count, stages, R, g);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = warp * 32 + lane;
+    if (wait_accumulator(R, g)) {
+        const uint32_t tbase = R.tmem_base + ((uint32_t)(warp * 32) << 16);
+        const int p = row < rows ? g.u_pairs[q0 + row] : 0;
+        const float wp = row < rows ? g.topk_w[p] : 0.f;
+        __nv_bfloat16 *dst = g.y + (size_t)p * H + n0;
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c0, r);
+            if (row < rows) {
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2)
+                    packed[i / 2] =
+                        (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[i]) * wp)) |
+                        ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[i + 1]) * wp)) << 16);
+                uint4 *d4 = reinterpret_cast<uint4 *>(dst + c0);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            }
+        }
+    }
+    tile_teardown(R, g);
+}
+
+// out[t] = sum over k in routing order of y[t * K + k], t in [t0, t1).
+__global__ void combine_kernel(const uint4 *y, int t0, int t1, int K, int H8, uint4 *out) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)(t1 - t0) * H8) return;
+    const int t = t0 + (int)(i / H8), c = (int)(i % H8);
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int k = 0; k < K; ++k) {
+        const uint4 v = y[((size_t)t * K + k) * H8 + c];
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            acc[2 * j] += bf16lo(wv[j]);
+            acc[2 * j + 1] += bf16hi(wv[j]);
+        }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        o[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * j])) |
+               ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * j + 1])) << 16);
+    out[(size_t)t * H8 + c] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---- host ----------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+void init_encode() {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn)
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    else
+        cudaGetLastError();
+}
+
+// Row-major bf16 matrix [rows][cols] (16-byte aligned base, cols % 8 == 0) as
+// 64 x 128 boxes with 128-byte swizzle.
+int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols) {
+    std::call_once(g_encode_once, init_encode);
+    if (!g_encode) return set_error("wisp: cuTensorMapEncodeTiled is not available"), WISP_ERR_UNSUPPORTED;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kHalfN};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error("wisp: cuTensorMapEncodeTiled failed"), WISP_ERR_CUDA;
+    return WISP_OK;
+}
+
+}  // namespace
+}  // namespace gemm
+
+bool prefill_shapes_supported(int H, int I) {
+    return H > 0 && I > 0 && H % gemm::kBN == 0 && I % gemm::kHalfN == 0;
+}
+
+int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
+    using namespace gemm;
+    if (!prefill_shapes_supported(p.H, p.I))
+        return set_error("wisp: prefill GEMM needs hidden % 256 == 0 and inter % 128 == 0"), WISP_ERR_UNSUPPORTED;
+    if (p.npairs <= 0 || p.nu <= 0) return WISP_OK;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    WISP_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return WISP_ERR_INVALID;
+    if (!attr_set[dev]) {
+        WISP_CUDA_TRY(cudaFuncSetAttribute(gateup_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        WISP_CUDA_TRY(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        attr_set[dev] = true;
+    }
+    CUtensorMap mx, mw13, mact, mw2;
+    int rc = make_map(&mx, p.x_perm, (uint64_t)p.perm_rows, (uint64_t)p.H);
+    if (!rc) rc = make_map(&mw13, p.w13, (uint64_t)p.slots * 2 * p.I, (uint64_t)p.H);
+    if (!rc) rc = make_map(&mact, p.act_perm, (uint64_t)p.perm_rows, (uint64_t)p.I);
+    if (!rc) rc = make_map(&mw2, p.w2, (uint64_t)p.slots * p.H, (uint64_t)p.I);
+    if (rc) return rc;
+    GroupGemm g{};
+    g.u_off = p.u_off;
+    g.u_pairs = p.u_pairs;
+    g.u_slot = p.u_slot;
+    g.nu = p.nu;
+    g.H = p.H;
+    g.I = p.I;
+    g.K = p.K;
+    g.topk_w = p.topk_w;
+    g.act_perm = p.act_perm;
+    g.y = p.y;
+    g.status = p.status;
+    g.wait_ns = p.wait_ns;
+    // tiles: at most one partial tile per expert beyond the full ones
+    const int mtiles = p.nu + (p.npairs + kBM - 1) / kBM;
+    const int warps = 8;
+    gather_kernel<<<(p.npairs + warps - 1) / warps, warps * 32, 0, stream>>>(
+        reinterpret_cast<const uint4 *>(p.x), p.u_pairs, p.npairs, p.K, p.H / 8, reinterpret_cast<uint4 *>(p.x_perm));
+    WISP_CUDA_TRY(cudaGetLastError());
+    gateup_gemm_kernel<<<dim3(mtiles, p.I / kHalfN), kThreads, kSmemBytes, stream>>>(mx, mw13, g);
+    WISP_CUDA_TRY(cudaGetLastError());
+    down_gemm_kernel<<<dim3(mtiles, p.H / kBN), kThreads, kSmemBytes, stream>>>(mact, mw2, g);
+    WISP_CUDA_TRY(cudaGetLastError());
+    const long n = (long)(p.t1 - p.t0) * (p.H / 8);
+    if (n > 0) {
+        combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(reinterpret_cast<const uint4 *>(p.y), p.t0,
+                                                                        p.t1, p.K, p.H / 8,
+                                                                        reinterpret_cast<uint4 *>(p.out));
+        WISP_CUDA_TRY(cudaGetLastError());
+    }
+    return WISP_OK;
+}
+
+}  // namespace wisp

@@ -43,6 +43,7 @@
 #include "decode.cuh"
 #include "forward.cuh"
 #include "pager.cuh"
+#include "prefill.cuh"
 
 namespace wisp {
 
@@ -113,6 +114,7 @@ struct wisp_layer {
             *d_u_slot = nullptr, *d_u_gen = nullptr, *d_u_off = nullptr, *d_u_pairs = nullptr,
             *d_counters = nullptr, *d_dev_hdr = nullptr;
     __nv_bfloat16 *d_act = nullptr, *d_y = nullptr;
+    __nv_bfloat16 *d_xperm = nullptr, *d_actperm = nullptr;  // prefill GEMM rows, expert-major
     int32_t *h_mb = nullptr, *d_mb = nullptr;  // kMbRing mailboxes of mb_words words
     long mb_words = 0;
     int mb_next = 0;
@@ -319,12 +321,13 @@ void free_ws(wisp_layer *L) {
     for (void *p : {(void *)L->d_slots, (void *)L->d_grp_start, (void *)L->d_grp_nu,
                     (void *)L->d_grp_nhit, (void *)L->d_u_slot,
                     (void *)L->d_u_gen, (void *)L->d_u_off, (void *)L->d_u_pairs, (void *)L->d_counters,
-                    (void *)L->d_dev_hdr, (void *)L->d_act, (void *)L->d_y})
+                    (void *)L->d_dev_hdr, (void *)L->d_act, (void *)L->d_y, (void *)L->d_xperm,
+                    (void *)L->d_actperm})
         cudaFree(p);
     if (L->h_mb) cudaFreeHost(L->h_mb);
     L->d_slots = L->d_grp_start = L->d_grp_nu = L->d_grp_nhit = L->d_u_slot = L->d_u_gen = L->d_u_off =
         L->d_u_pairs = L->d_counters = L->d_dev_hdr = nullptr;
-    L->d_act = L->d_y = nullptr;
+    L->d_act = L->d_y = L->d_xperm = L->d_actperm = nullptr;
     L->h_mb = L->d_mb = nullptr;
     L->wsT = -1;
     L->wsK = 0;
@@ -361,6 +364,10 @@ int ensure_ws(wisp_layer *L, int T, int K) {
         WISP_CUDA_TRY(cudaMalloc(&L->d_act, sizeof(__nv_bfloat16) * 2 * P * I));
         L->act_dirty = true;
         WISP_CUDA_TRY(cudaMalloc(&L->d_y, sizeof(__nv_bfloat16) * P * H));
+        if (prefill_shapes_supported(L->H, L->I)) {
+            WISP_CUDA_TRY(cudaMalloc(&L->d_xperm, sizeof(__nv_bfloat16) * P * H));
+            WISP_CUDA_TRY(cudaMalloc(&L->d_actperm, sizeof(__nv_bfloat16) * P * I));
+        }
     }
     const long words = (mailbox_words(nT, nK) + 31) & ~31L;
     WISP_CUDA_TRY(cudaHostAlloc(&L->h_mb, sizeof(int32_t) * words * kMbRing, cudaHostAllocMapped));
@@ -512,6 +519,15 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
     return WISP_OK;
 }
 
+// Calls above the decode kernels' range (T * k > 256) run their expert
+// compute as tensor-core grouped GEMMs where the shapes allow.  The choice
+// depends on the call's size only (not on its grouping), so outputs stay
+// byte-identical across caps and slot placements.
+constexpr int kPrefillMinPairs = 257;
+bool use_prefill_gemm(const wisp_layer *L, int T, int K) {
+    return (long)T * K >= kPrefillMinPairs && prefill_shapes_supported(L->H, L->I) && L->d_xperm;
+}
+
 // Synchronous path after run_pager: page-ins per group (write-after-read via
 // group events) and, when `compute` is set, the per-group decode kernels.
 int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K, void *out,
@@ -540,7 +556,36 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
             WISP_CUDA_TRY(cudaEventRecord(L->ev_copy[g], L->copy_stream));
             WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copy[g], 0));
         }
-        if (compute && t1 > t0 && nu[g] > 0) {
+        if (compute && t1 > t0 && nu[g] > 0 && use_prefill_gemm(L, T, K)) {
+            // tensor-core grouped GEMMs (gather, gate-up + SiLU-mul, down, combine)
+            const int64_t p0 = (int64_t)t0 * K;
+            PrefillGroup pg{};
+            pg.x = reinterpret_cast<const __nv_bfloat16 *>(x);
+            pg.w13 = reinterpret_cast<const __nv_bfloat16 *>(L->d13);
+            pg.w2 = reinterpret_cast<const __nv_bfloat16 *>(L->d2);
+            pg.slots = L->cap;
+            pg.u_off = L->d_u_off + p0 + g;
+            pg.u_pairs = L->d_u_pairs + p0;
+            pg.u_slot = L->d_u_slot + p0;
+            pg.nu = nu[g];
+            pg.npairs = (t1 - t0) * K;
+            pg.t0 = t0;
+            pg.t1 = t1;
+            pg.K = K;
+            pg.H = L->H;
+            pg.I = L->I;
+            pg.topk_w = w;
+            pg.x_perm = L->d_xperm;
+            pg.act_perm = L->d_actperm;
+            pg.perm_rows = L->wsT * L->wsK;
+            pg.y = L->d_y;
+            pg.out = reinterpret_cast<__nv_bfloat16 *>(out);
+            pg.status = L->d_status;
+            pg.wait_ns = L->wait_ns;
+            rc = launch_prefill_group(pg, stream);
+            if (rc) return rc;
+            L->launches += kPrefillKernelsPerGroup;
+        } else if (compute && t1 > t0 && nu[g] > 0) {
             const int64_t p0 = (int64_t)t0 * K;
             GroupCompute gc{};
             gc.x = reinterpret_cast<const __nv_bfloat16 *>(x);
@@ -780,7 +825,7 @@ int wisp_moe_forward(wisp_layer *L, const void *x, const float *topk_weights,
     int rc = take_errors(L);
     if (rc) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (L->async && top_k <= L->cap)
+    if (L->async && top_k <= L->cap && !use_prefill_gemm(L, num_tokens, top_k))
         return forward_async(L, x, topk_weights, topk_ids, ids_int64, num_tokens, top_k, out, s);
     rc = run_pager(L, topk_ids, ids_int64, num_tokens, top_k, 0, 1, s);
     if (rc) return rc;

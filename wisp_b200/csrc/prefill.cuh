@@ -1,0 +1,37 @@
+// Prefill (large token groups) expert compute on tcgen05 tensor cores.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wisp {
+
+// One token group whose experts are resident in their slots.
+struct PrefillGroup {
+    const __nv_bfloat16 *x;         // [T][H] hidden states
+    const __nv_bfloat16 *w13;       // slot scratch [slots][2I][H]
+    const __nv_bfloat16 *w2;        // slot scratch [slots][H][I]
+    int slots;                      // slot count (tensor-map extent)
+    const int32_t *u_off;           // [nu + 1] group-local offsets into u_pairs
+    const int32_t *u_pairs;         // [npairs] absolute pair index t * K + k, expert-major
+    const int32_t *u_slot;          // [nu]
+    int nu, npairs;
+    int t0, t1, K, H, I;
+    const float *topk_w;            // [T * K]
+    __nv_bfloat16 *x_perm;          // [perm_rows][H] workspace
+    __nv_bfloat16 *act_perm;        // [perm_rows][I] workspace
+    int perm_rows;                  // rows of the two workspaces (>= npairs)
+    __nv_bfloat16 *y;               // [T * K][H]
+    __nv_bfloat16 *out;             // [T][H]
+    int *status;                    // sticky status word
+    long long wait_ns;
+};
+
+// The tensor-core path covers hidden % 256 == 0 and inter % 128 == 0.
+bool prefill_shapes_supported(int H, int I);
+
+// Launches gather, gate-up GEMM, down GEMM and combine (4 kernels) on `stream`.
+constexpr int kPrefillKernelsPerGroup = 4;
+int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream);
+
+}  // namespace wisp
