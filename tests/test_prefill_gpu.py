@@ -1,10 +1,15 @@
 """Prefill-sized calls (T * k > 256) on the tcgen05 tensor-core path: parity
-with the fp32 CPU oracle (same tolerance as the decode tests: max-abs <= 1e-2,
-mean-rel <= 1e-3 against the oracle with the reference's bf16 storage
-points), byte identity across caps, slot placements and resident/paged
-modes (the path depends on the call size only), the pager state unchanged by
-the path, and the kernel count (pager + gather, gate-up, down, combine per
-token group)."""
+with the fp32 CPU oracle with the reference's bf16 storage points (h, a, each
+weighted y and the output are stored bf16): mean-rel <= 1e-3 as in the decode
+tests, and per element |out - ref| <= max(1e-2, 2 ulp(out) + sum over k of
+2 ulp(y_k)).  With another fp32 accumulation order each stored value may round
+the other way, and the output sums the stored y_k: at the larger hidden and
+intermediate sizes of Qwen3-235B the y_k reach 1..4 (one bf16 ulp 0.008..0.016)
+while their sum may be small, so a fixed 1e-2 bound cannot hold there for any
+bf16-storing implementation; at the Qwen3-30B-A3B shapes the 1e-2 term decides.
+Also: byte identity across caps, slot placements and resident/paged modes (the
+path depends on the call size only), the pager state unchanged by the path,
+and the kernel count (pager + gather, gate-up, down, combine per token group)."""
 import pytest
 import torch
 
@@ -27,9 +32,16 @@ def test_prefill_matches_oracle(E, H, I, T, K, cap, mode):
     w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=T + H)
     st = state(w13, w2, cap, mode)
     out = fwd(st, x, w, ids)
-    ref = moe_reference(x, w13, w2, w, ids)
+    ref, Y = moe_reference(x, w13, w2, w, ids, return_partials=True)
     c = compare(out, ref)
-    assert c["max_abs"] <= MAX_ABS and c["mean_rel"] <= MEAN_REL, c
+    assert c["mean_rel"] <= MEAN_REL, c
+
+    def ulp(v):  # bf16: 8 significand bits
+        return torch.ldexp(torch.ones_like(v), torch.frexp(v.abs().clamp_min(1e-30))[1] - 8)
+
+    bound = torch.clamp_min(2 * ulp(ref) + (2 * ulp(Y)).sum(dim=1), MAX_ABS)
+    d = (out.float() - ref).abs()
+    assert bool((d <= bound).all()), (c, float((d - bound).max()))
     assert torch.equal(fwd(st, x, w, ids), out)
     st.close()
 
