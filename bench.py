@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--cap", type=int, default=32)
     ap.add_argument("--layers", type=int, default=SHAPE.layers)
     ap.add_argument("--no-resident", action="store_true", help="skip the resident-decode phase")
-    ap.add_argument("--phase", default="all", choices=["all", "resident"],
+    ap.add_argument("--phase", default="all", choices=["all", "resident", "prefill"],
                     help="'resident' runs only the resident-decode region (profiling: the paged "
                          "forward waits on page-ins a host thread issues during the launch, which "
                          "a kernel-serialising profiler would stall)")
@@ -184,6 +184,8 @@ def run_wisp(args):
     total = args.warmup + args.steps
     if args.phase == "resident":
         return resident_only(args, dev, hbm_peak, peak_src)
+    if args.phase == "prefill":
+        return prefill_only(args, dev, hbm_peak, peak_src)
     t0 = time.time()
     masters = make_masters(L, dev)
     states = [WispMoEState(h13, h2, C, "paged", dev, i) for i, (h13, h2) in enumerate(masters)]
@@ -328,6 +330,63 @@ def resident_only(args, dev, hbm_peak, peak_src):
                          "peak": hbm_peak, "unit": "GB/s", "frac": r["frac"], "peak_src": peak_src,
                          "bytes_per_launch": r["bytes_per_launch"], "us_per_launch": r["us_per_launch"]},
             "resident_decode": r}
+
+
+def prefill_only(args, dev, hbm_peak, peak_src):
+    """Config 3's prefill chunk on resident layers (cap = E): T = 2048 tokens,
+    uniform top-8 of 128 (every expert touched), one forward per layer on the
+    tcgen05 tensor-core path; reports tensor TFLOP/s (2 T k 3 H I per layer)
+    and the expert-weight HBM GB/s against the measured peaks."""
+    from wisp_b200.integrations.vllm.fused_moe import WispMoEState
+    tflops_peak = 1680.6
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tflops_peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    L = min(args.layers, 8)
+    T = 2048
+    masters = make_masters(L, dev)
+    states = []
+    for i in range(L):
+        st = WispMoEState(masters[i][0], masters[i][1], SHAPE.experts, "resident", dev, i)
+        st.prime_identity()
+        states.append(st)
+    x = wl.hidden_states(T, SHAPE.hidden, seed=3).to(dev)
+    out = torch.empty_like(x)
+    routes = []
+    for s in range(args.warmup + args.steps):
+        ids, w = wl.uniform_topk(T, SHAPE.experts, SHAPE.top_k, seed=100 + s)
+        routes.append((torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)))
+    for s in range(args.warmup):
+        for layer in range(L):
+            states[layer].forward(x, routes[s][1], routes[s][0], out=out)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(args.warmup, args.warmup + args.steps):
+        for layer in range(L):
+            states[layer].forward(x, routes[s][1], routes[s][0], out=out)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    n = args.steps * L
+    us = ms * 1e3 / n
+    flop = 2.0 * T * SHAPE.top_k * 3 * SHAPE.hidden * SHAPE.inter
+    wbytes = SHAPE.experts * SHAPE.expert_bytes
+    for st in states:
+        st.close()
+    tf = flop / (us * 1e-6) / 1e12
+    gbs = wbytes / (us * 1e-6) / 1e9
+    roof_us = max(flop / (tflops_peak * 1e12), wbytes / (hbm_peak * 1e9)) * 1e6
+    return {"metric": "prefill tok/s (resident, 2048-token chunk)", "value": T * args.steps / (ms * 1e-3 / L) / L,
+            "unit": "tok/s per layer stack of %d" % L, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic (uniform top-8 routing)",
+            "config": {"workload": f"qwen3-30b-a3b prefill, {L} resident layers, T {T}, uniform top-8"},
+            "prefill": {"us_per_layer": us, "tflops": tf, "tflops_peak": tflops_peak,
+                        "tensor_frac": tf / tflops_peak, "weight_gbs": gbs, "hbm_peak_gbs": hbm_peak,
+                        "hbm_frac": gbs / hbm_peak, "roofline_us": roof_us, "roofline_frac": roof_us / us,
+                        "peak_src": peak_src}}
 
 
 def resident_phase(args, masters, dev, hbm_peak, batch):
@@ -607,7 +666,7 @@ def main():
         return
     line = run_wisp(args)
     if rank == 0:
-        if args.gpus == 1 and args.cpu_sample_s > 0:
+        if args.gpus == 1 and args.cpu_sample_s > 0 and args.phase == "all":
             line["cpu_baseline"] = run_reference(args)
         print(json.dumps(line))
 

@@ -25,11 +25,26 @@ __global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int
 
 // Setup common to both GEMMs: tile lookup, barriers, TMEM.  Returns false when
 // this CTA has no tile.
+constexpr int kMaxTileExperts = 1024;
 __device__ __forceinline__ bool tile_setup(const GroupGemm &g, Ring &R, int &u, int &q0, int &rows) {
     __shared__ int s_u, s_q0, s_rows;
+    __shared__ int s_off[kMaxTileExperts + 1];
+    // the group's offsets in one round of loads, then a scan in shared memory
+    const int nu = min(g.nu, kMaxTileExperts);
+    for (int i = threadIdx.x; i <= nu; i += blockDim.x) s_off[i] = g.u_off[i];
+    __syncthreads();
     if (threadIdx.x == 0) {
-        int uu = -1, qq = 0, rr = 0;
-        if (!find_mtile(g, blockIdx.x, uu, qq, rr)) uu = -1;
+        int uu = -1, qq = 0, rr = 0, bm = blockIdx.x;
+        for (int e = 0; e < nu; ++e) {
+            const int nt = (s_off[e + 1] - s_off[e] + kBM - 1) / kBM;
+            if (bm < nt) {
+                uu = e;
+                qq = s_off[e] + bm * kBM;
+                rr = min(kBM, s_off[e + 1] - qq);
+                break;
+            }
+            bm -= nt;
+        }
         s_u = uu;
         s_q0 = qq;
         s_rows = rr;

@@ -166,23 +166,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
            | ((uint32_t)(M >> 4) << 24);// M / 16
 }
 
-// The bm-th 128-pair tile over the group's experts: its expert, first pair
-// position and rows; false when bm is past the last tile.
-__device__ __forceinline__ bool find_mtile(const GroupGemm &g, int bm, int &u, int &q0, int &rows) {
-    for (int e = 0; e < g.nu; ++e) {
-        const int a = g.u_off[e], b = g.u_off[e + 1];
-        const int nt = (b - a + kBM - 1) / kBM;
-        if (bm < nt) {
-            u = e;
-            q0 = a + bm * kBM;
-            rows = min(kBM, b - q0);
-            return true;
-        }
-        bm -= nt;
-    }
-    return false;
-}
-
 // The status word is mapped host memory: a plain store (any non-zero code
 // marks the failure; no atomics across PCIe).
 __device__ __forceinline__ void record_timeout(const GroupGemm &g) {
