@@ -3,6 +3,7 @@
 #include "gemm_sm100.cuh"
 #include "prefill.cuh"
 
+#include <algorithm>
 #include <mutex>
 
 namespace wisp {
@@ -23,54 +24,71 @@ __global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int
     for (int c = threadIdx.x & 31; c < H8; c += 32) dst[c] = src[c];
 }
 
-// Setup common to both GEMMs: tile lookup, barriers, TMEM.  Returns false when
-// this CTA has no tile.
+// The group's experts and their 128-pair tiles, in shared memory.
 constexpr int kMaxTileExperts = 1024;
-__device__ __forceinline__ bool tile_setup(const GroupGemm &g, Ring &R, int &u, int &q0, int &rows) {
-    __shared__ int s_u, s_q0, s_rows;
-    __shared__ int s_off[kMaxTileExperts + 1];
-    // the group's offsets in one round of loads, then a scan in shared memory
+struct TileTable {
+    int nu, mtiles;
+    int off[kMaxTileExperts + 1];  // pair-list offsets
+    int mt[kMaxTileExperts + 1];   // first tile of each expert (prefix of tile counts)
+};
+
+// Tile m -> expert u, first list position q0, rows (binary search: the last
+// expert whose first tile is <= m; every expert of a group has pairs).
+__device__ __forceinline__ void tile_of(const TileTable &tt, int m, int &u, int &q0, int &rows) {
+    int lo = 0, hi = tt.nu - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (tt.mt[mid] <= m)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    u = lo;
+    q0 = tt.off[u] + (m - tt.mt[u]) * kBM;
+    rows = min(kBM, tt.off[u + 1] - q0);
+}
+
+// Setup of a persistent GEMM CTA: tile table, barriers, TMEM (both
+// accumulators).  Returns the number of tiles (n_cols tiles per m tile); a CTA
+// with none returns 0 before allocating anything.
+__device__ __forceinline__ int gemm_setup(const GroupGemm &g, int n_cols, TileTable &tt, Ring &R) {
     const int nu = min(g.nu, kMaxTileExperts);
-    for (int i = threadIdx.x; i <= nu; i += blockDim.x) s_off[i] = g.u_off[i];
+    for (int i = threadIdx.x; i <= nu; i += blockDim.x) tt.off[i] = g.u_off[i];
     __syncthreads();
     if (threadIdx.x == 0) {
-        int uu = -1, qq = 0, rr = 0, bm = blockIdx.x;
+        tt.nu = nu;
+        int acc = 0;
         for (int e = 0; e < nu; ++e) {
-            const int nt = (s_off[e + 1] - s_off[e] + kBM - 1) / kBM;
-            if (bm < nt) {
-                uu = e;
-                qq = s_off[e] + bm * kBM;
-                rr = min(kBM, s_off[e + 1] - qq);
-                break;
-            }
-            bm -= nt;
+            tt.mt[e] = acc;
+            acc += (tt.off[e + 1] - tt.off[e] + kBM - 1) / kBM;
         }
-        s_u = uu;
-        s_q0 = qq;
-        s_rows = rr;
+        tt.mt[nu] = acc;
+        tt.mtiles = acc;
         R.abort = 0;
         R.issued = R.consumed = 0;
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&R.full[s], 1);
             mbar_init(&R.empty[s], 1);
         }
-        mbar_init(&R.tmem_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&R.acc_full[b], 1);
+            mbar_init(&R.acc_empty[b], kEpiThreads);
+        }
+        mbar_init(&R.mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     __syncthreads();
-    u = s_u;
-    q0 = s_q0;
-    rows = s_rows;
-    if (u < 0) return false;
+    const int ntiles = tt.mtiles * n_cols;
+    if ((int)blockIdx.x >= ntiles) return 0;
     if ((threadIdx.x >> 5) == 0) tmem_alloc(&R.tmem_base, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    return true;
+    return ntiles;
 }
 
-__device__ __forceinline__ void tile_teardown(Ring &R, const GroupGemm &g) {
+__device__ __forceinline__ void gemm_teardown(Ring &R, const GroupGemm &g) {
     tc_fence_before();
     __syncthreads();
     if (R.abort) drain_ring(R, g);
@@ -79,100 +97,140 @@ __device__ __forceinline__ void tile_teardown(Ring &R, const GroupGemm &g) {
     if ((threadIdx.x >> 5) == 0) tmem_dealloc(R.tmem_base, kTmemCols);
 }
 
-// Epilogue wait for the accumulator (all threads); false after an abort.  The
-// result is uniform over the warp and the warp leaves converged, as the
-// .sync.aligned TMEM loads that follow require (lanes 0 of warps 0 and 1 come
-// from the producer and MMA loops).
-__device__ __forceinline__ bool wait_accumulator(Ring &R, const GroupGemm &g) {
+// Epilogue side of tile i (warps 2..5): wait for its accumulator; false after
+// an abort.  Uniform over the warp, which leaves converged for the
+// .sync.aligned TMEM loads.
+__device__ __forceinline__ bool wait_acc(Ring &R, int i, const GroupGemm &g) {
     volatile int *abort = &R.abort;
-    const bool ok = mbar_wait(&R.tmem_full, 0, g.wait_ns, abort) && !*abort;
+    const bool ok = mbar_wait(&R.acc_full[i & 1], (i / 2) & 1, g.wait_ns, abort) && !*abort;
     const bool all = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     return all;
 }
+__device__ __forceinline__ void release_acc(Ring &R, int i) {
+    tc_fence_before();
+    mbar_arrive(&R.acc_empty[i & 1]);
+}
 
-// Gate-up + SiLU-mul: grid (m tiles, I / 128).
+// Gate-up + SiLU-mul, persistent: tiles (m, n) with n over I / 128 fastest.
 __global__ void __launch_bounds__(kThreads, 1)
     gateup_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w13,
                        GroupGemm g) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ Ring R;
+    __shared__ TileTable tt;
     unsigned char *stages = align1024(smem_raw);
-    int u, q0, rows;
-    if (!tile_setup(g, R, u, q0, rows)) return;
-    const int I = g.I, j0 = blockIdx.y * kHalfN;
-    const int slot_row = g.u_slot[u] * 2 * I;
+    const int I = g.I, n_cols = I / kHalfN;
+    const int ntiles = gemm_setup(g, n_cols, tt, R);
+    if (ntiles == 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kb_count = g.H / kBK;
-    mainloop(&map_x, &map_w13, q0, slot_row + j0, slot_row + I + j0, kb_count, stages, R, g);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = warp * 32 + lane;
-    if (wait_accumulator(R, g)) {
-        const uint32_t tbase = R.tmem_base + ((uint32_t)(warp * 32) << 16);
-        __nv_bfloat16 *dst = g.act_perm + (size_t)(q0 + row) * I + j0;
-        for (int c0 = 0; c0 < kHalfN; c0 += 32) {
-            uint32_t gr[32], ur[32];
-            tmem_ld32(tbase + c0, gr);
-            tmem_ld32(tbase + kHalfN + c0, ur);
-            if (row < rows) {
-                uint32_t packed[16];
+    if (warp == 0) {
+        if (lane == 0)
+            produce(&map_x, &map_w13, ntiles, kb_count, stages, R, g, [&](int t) {
+                int u, q0, rows;
+                tile_of(tt, t / n_cols, u, q0, rows);
+                const int slot_row = g.u_slot[u] * 2 * I, j0 = (t % n_cols) * kHalfN;
+                return TileOperands{q0, slot_row + j0, slot_row + I + j0};
+            });
+    } else if (warp == 1) {
+        if (lane == 0) issue_mmas(ntiles, kb_count, stages, R, g);
+    } else {
+        const int quarter = warp & 3, row = quarter * 32 + lane;
+        int i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+            if (!wait_acc(R, i, g)) break;
+            int u, q0, rows;
+            tile_of(tt, t / n_cols, u, q0, rows);
+            const int j0 = (t % n_cols) * kHalfN;
+            const uint32_t tbase = R.tmem_base + (i & 1) * kAccCols + ((uint32_t)(quarter * 32) << 16);
+            __nv_bfloat16 *dst = g.act_perm + (size_t)(q0 + row) * I + j0;
+            for (int c0 = 0; c0 < kHalfN; c0 += 32) {
+                uint32_t gr[32], ur[32];
+                tmem_ld32(tbase + c0, gr);
+                tmem_ld32(tbase + kHalfN + c0, ur);
+                if (row < rows) {
+                    uint32_t packed[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    float o[2];
+                    for (int k = 0; k < 32; k += 2) {
+                        float o[2];
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const float gv = round_bf16(__uint_as_float(gr[i + h]));
-                        const float uv = round_bf16(__uint_as_float(ur[i + h]));
-                        o[h] = gv / (1.0f + expf(-gv)) * uv;
+                        for (int h = 0; h < 2; ++h) {
+                            const float gv = round_bf16(__uint_as_float(gr[k + h]));
+                            const float uv = round_bf16(__uint_as_float(ur[k + h]));
+                            o[h] = gv / (1.0f + expf(-gv)) * uv;
+                        }
+                        packed[k / 2] = (uint32_t)__bfloat16_as_ushort(act_value(o[0])) |
+                                        ((uint32_t)__bfloat16_as_ushort(act_value(o[1])) << 16);
                     }
-                    packed[i / 2] = (uint32_t)__bfloat16_as_ushort(act_value(o[0])) |
-                                    ((uint32_t)__bfloat16_as_ushort(act_value(o[1])) << 16);
-                }
-                uint4 *d4 = reinterpret_cast<uint4 *>(dst + c0);
+                    uint4 *d4 = reinterpret_cast<uint4 *>(dst + c0);
 #pragma unroll
-                for (int v = 0; v < 4; ++v)
-                    d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                    for (int v = 0; v < 4; ++v)
+                        d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                }
             }
+            release_acc(R, i);
         }
     }
-    tile_teardown(R, g);
+    gemm_teardown(R, g);
 }
 
-// Down x routing weight: grid (m tiles, H / 256).
+// Down x routing weight, persistent: tiles (m, n) with n over H / 256 fastest.
 __global__ void __launch_bounds__(kThreads, 1)
     down_gemm_kernel(const __grid_constant__ CUtensorMap map_act, const __grid_constant__ CUtensorMap map_w2,
                      GroupGemm g) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ Ring R;
+    __shared__ TileTable tt;
     unsigned char *stages = align1024(smem_raw);
-    int u, q0, rows;
-    if (!tile_setup(g, R, u, q0, rows)) return;
-    const int H = g.H, n0 = blockIdx.y * kBN;
-    const int slot_row = g.u_slot[u] * H;
+    const int H = g.H, n_cols = H / kBN;
+    const int ntiles = gemm_setup(g, n_cols, tt, R);
+    if (ntiles == 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kb_count = g.I / kBK;
-    mainloop(&map_act, &map_w2, q0, slot_row + n0, slot_row + n0 + kHalfN, kb_count, stages, R, g);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = warp * 32 + lane;
-    if (wait_accumulator(R, g)) {
-        const uint32_t tbase = R.tmem_base + ((uint32_t)(warp * 32) << 16);
-        const int p = row < rows ? g.u_pairs[q0 + row] : 0;
-        const float wp = row < rows ? g.topk_w[p] : 0.f;
-        __nv_bfloat16 *dst = g.y + (size_t)p * H + n0;
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(tbase + c0, r);
-            if (row < rows) {
-                uint32_t packed[16];
+    if (warp == 0) {
+        if (lane == 0)
+            produce(&map_act, &map_w2, ntiles, kb_count, stages, R, g, [&](int t) {
+                int u, q0, rows;
+                tile_of(tt, t / n_cols, u, q0, rows);
+                const int slot_row = g.u_slot[u] * H, n0 = (t % n_cols) * kBN;
+                return TileOperands{q0, slot_row + n0, slot_row + n0 + kHalfN};
+            });
+    } else if (warp == 1) {
+        if (lane == 0) issue_mmas(ntiles, kb_count, stages, R, g);
+    } else {
+        const int quarter = warp & 3, row = quarter * 32 + lane;
+        int i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+            if (!wait_acc(R, i, g)) break;
+            int u, q0, rows;
+            tile_of(tt, t / n_cols, u, q0, rows);
+            const int n0 = (t % n_cols) * kBN;
+            const uint32_t tbase = R.tmem_base + (i & 1) * kAccCols + ((uint32_t)(quarter * 32) << 16);
+            const int p = row < rows ? g.u_pairs[q0 + row] : 0;
+            const float wp = row < rows ? g.topk_w[p] : 0.f;
+            __nv_bfloat16 *dst = g.y + (size_t)p * H + n0;
+            for (int c0 = 0; c0 < kBN; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c0, r);
+                if (row < rows) {
+                    uint32_t packed[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 2)
-                    packed[i / 2] =
-                        (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[i]) * wp)) |
-                        ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[i + 1]) * wp)) << 16);
-                uint4 *d4 = reinterpret_cast<uint4 *>(dst + c0);
+                    for (int k = 0; k < 32; k += 2)
+                        packed[k / 2] =
+                            (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[k]) * wp)) |
+                            ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[k + 1]) * wp))
+                             << 16);
+                    uint4 *d4 = reinterpret_cast<uint4 *>(dst + c0);
 #pragma unroll
-                for (int v = 0; v < 4; ++v)
-                    d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                    for (int v = 0; v < 4; ++v)
+                        d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                }
             }
+            release_acc(R, i);
         }
     }
-    tile_teardown(R, g);
+    gemm_teardown(R, g);
 }
 
 // out[t] = sum over k in routing order of y[t * K + k], t in [t0, t1).
@@ -273,15 +331,20 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
     g.y = p.y;
     g.status = p.status;
     g.wait_ns = p.wait_ns;
-    // tiles: at most one partial tile per expert beyond the full ones
-    const int mtiles = p.nu + (p.npairs + kBM - 1) / kBM;
+    // persistent grids: at most one CTA per SM (tiles: at most one partial
+    // 128-pair tile per expert beyond the full ones)
+    int sms = 0;
+    WISP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const long mtiles = (long)p.nu + (p.npairs + kBM - 1) / kBM;
+    const int grid_gu = (int)std::min<long>(mtiles * (p.I / kHalfN), sms);
+    const int grid_dn = (int)std::min<long>(mtiles * (p.H / kBN), sms);
     const int warps = 8;
     gather_kernel<<<(p.npairs + warps - 1) / warps, warps * 32, 0, stream>>>(
         reinterpret_cast<const uint4 *>(p.x), p.u_pairs, p.npairs, p.K, p.H / 8, reinterpret_cast<uint4 *>(p.x_perm));
     WISP_CUDA_TRY(cudaGetLastError());
-    gateup_gemm_kernel<<<dim3(mtiles, p.I / kHalfN), kThreads, kSmemBytes, stream>>>(mx, mw13, g);
+    gateup_gemm_kernel<<<grid_gu, kThreads, kSmemBytes, stream>>>(mx, mw13, g);
     WISP_CUDA_TRY(cudaGetLastError());
-    down_gemm_kernel<<<dim3(mtiles, p.H / kBN), kThreads, kSmemBytes, stream>>>(mact, mw2, g);
+    down_gemm_kernel<<<grid_dn, kThreads, kSmemBytes, stream>>>(mact, mw2, g);
     WISP_CUDA_TRY(cudaGetLastError());
     const long n = (long)(p.t1 - p.t0) * (p.H / 8);
     if (n > 0) {

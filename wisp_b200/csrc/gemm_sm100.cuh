@@ -16,17 +16,21 @@
 //               y[pair][h] = bf16(D * routing weight);
 //   combine     out[t] = sum over k in routing order of y[t*K + k] (fp32, bf16).
 //
-// Kernel structure (one CTA of 4 warps per output tile, one tile per CTA):
-// warp 0 lane 0 issues the TMA loads of a 4-stage ring (A tile 128 x 64 and
-// B tile 256 x 64 bf16 per stage, 128-byte swizzle, the canonical K-major
-// layout of the MMA's shared-memory descriptors), warp 1 lane 0 issues
-// tcgen05.mma (M 128, N 256, K 16) into a 256-column TMEM accumulator and
-// commits each stage back to the producer's "empty" barrier, and all four
-// warps read the accumulator back with tcgen05.ld (warp w owns TMEM lanes
-// 32w..32w+31 = tile rows) for the epilogue.  Every wait is bounded by a
-// %globaltimer limit; a wait that runs out records WISP_ERR_TIMEOUT in the
-// status word, the CTA waits (bounded) for its copies and MMAs in flight,
-// frees its tensor memory and returns.
+// Kernel structure (persistent: at most one CTA of 6 warps per SM, each
+// looping over output tiles in N-fastest order, so consecutive tiles share the
+// token rows and one expert's weights stay in L2): warp 0 lane 0 issues the
+// TMA loads of a 4-stage ring (A tile 128 x 64 and B tile 256 x 64 bf16 per
+// stage, 128-byte swizzle, the canonical K-major layout of the MMA's
+// shared-memory descriptors) continuously across tiles; warp 1 lane 0 issues
+// tcgen05.mma (M 128, N 256, K 16) into one of two 256-column TMEM
+// accumulators and commits each stage back to the producer's "empty" barrier
+// and each finished accumulator to the epilogue; warps 2..5 read an
+// accumulator back with tcgen05.ld (warp w owns TMEM lanes 32 (w % 4) ..,
+// = tile rows) while the next tile accumulates into the other one.  Every
+// wait is bounded by a %globaltimer limit; a wait that runs out records
+// WISP_ERR_TIMEOUT in the status word, the roles stop, the CTA waits
+// (bounded) for its copies and MMAs in flight, frees its tensor memory and
+// returns.
 //
 // Per (pair, row) arithmetic is independent of which other pairs share a tile
 // (each accumulator element is its own dot product, K blocks in order), so
@@ -48,12 +52,14 @@ constexpr int kBK = 64;                        // K per stage: one 128-byte swiz
 constexpr int kBN = 256;                       // output columns per tile
 constexpr int kHalfN = kBN / 2;                // one TMA box of B rows
 constexpr int kStages = 4;
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;                  // producer warp, MMA warp, 4 epilogue warps
+constexpr int kEpiThreads = 128;
 constexpr int kATileBytes = kBM * kBK * 2;     // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 2;     // 32 KB
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
 constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + slack to align stages to 1024 B
-constexpr int kTmemCols = 256;
+constexpr int kAccCols = 256;                  // one accumulator
+constexpr int kTmemCols = 2 * kAccCols;         // two, double-buffered
 
 // Everything a group's GEMM kernels need besides the tensor maps.
 struct GroupGemm {
@@ -105,6 +111,22 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
             "r"(s_addr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s_addr(bar))
         : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_hint(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;" ::"r"(s_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s_addr(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_addr(bar)) : "memory");
 }
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t cols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_addr(dst_smem)),
@@ -172,58 +194,84 @@ __device__ __forceinline__ void record_timeout(const GroupGemm &g) {
     if (g.status) *reinterpret_cast<volatile int *>(g.status) = WISP_ERR_TIMEOUT;
 }
 
-// Mainloop shared by both GEMMs: A rows [a_row, +128) of map_a, B rows
-// [b_row0, +128) and [b_row1, +128) of map_b, K = kb_count * 64.  Leaves the
-// accumulator complete in TMEM (tmem_full arrives) unless it aborts.
+// Shared state of a persistent GEMM CTA.
 struct Ring {
-    uint64_t full[kStages], empty[kStages], tmem_full;
+    uint64_t full[kStages], empty[kStages];
+    uint64_t acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     int abort;
-    int issued, consumed;  // stages the producer filled / the MMA thread took
+    int issued, consumed;  // k-steps the producer filled / the MMA thread took
 };
 
-__device__ __forceinline__ void mainloop(const CUtensorMap *map_a, const CUtensorMap *map_b, int a_row, int b_row0,
-                                         int b_row1, int kb_count, unsigned char *stages, Ring &R,
-                                         const GroupGemm &g) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// A tile's operands: A rows [a_row, +128), B rows [b_row0, +128) and
+// [b_row1, +128), K = kb_count * 64.
+struct TileOperands {
+    int a_row, b_row0, b_row1;
+};
+
+// Producer (warp 0 lane 0): fills the ring for every tile of this CTA.
+template <class TileFn>
+__device__ __forceinline__ void produce(const CUtensorMap *map_a, const CUtensorMap *map_b, int ntiles, int kb_count,
+                                        unsigned char *stages, Ring &R, const GroupGemm &g, TileFn tile_operands) {
     volatile int *abort = &R.abort;
-    if (warp == 0 && lane == 0) {
-        // producer: TMA into the ring
-        for (int kb = 0; kb < kb_count; ++kb) {
-            const int s = kb % kStages;
-            if (kb >= kStages && !mbar_wait(&R.empty[s], ((kb / kStages) - 1) & 1, g.wait_ns, abort)) {
+    const uint64_t keep = policy_evict_last();  // token rows: reused by the tile's other N columns
+    int kstep = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const TileOperands op = tile_operands(t);
+        for (int kb = 0; kb < kb_count; ++kb, ++kstep) {
+            const int s = kstep % kStages;
+            if (kstep >= kStages && !mbar_wait(&R.empty[s], ((kstep / kStages) - 1) & 1, g.wait_ns, abort)) {
                 R.abort = 1;
                 record_timeout(g);
-                break;
+                return;
             }
             unsigned char *st = stages + s * kStageBytes;
             mbar_expect_tx(&R.full[s], kStageBytes);
-            tma_load_2d(st, map_a, kb * kBK, a_row, &R.full[s]);
-            tma_load_2d(st + kATileBytes, map_b, kb * kBK, b_row0, &R.full[s]);
-            tma_load_2d(st + kATileBytes + kHalfN * kBK * 2, map_b, kb * kBK, b_row1, &R.full[s]);
-            R.issued = kb + 1;
+            tma_load_2d_hint(st, map_a, kb * kBK, op.a_row, &R.full[s], keep);
+            tma_load_2d(st + kATileBytes, map_b, kb * kBK, op.b_row0, &R.full[s]);
+            tma_load_2d(st + kATileBytes + kHalfN * kBK * 2, map_b, kb * kBK, op.b_row1, &R.full[s]);
+            R.issued = kstep + 1;
         }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        const uint32_t idesc = idesc_bf16_f32(kBM, kBN);
-        for (int kb = 0; kb < kb_count; ++kb) {
-            const int s = kb % kStages;
-            if (!mbar_wait(&R.full[s], (kb / kStages) & 1, g.wait_ns, abort)) {
+    }
+}
+
+// MMA issuer (warp 1 lane 0): accumulates tile i into accumulator i % 2.
+__device__ __forceinline__ void issue_mmas(int ntiles, int kb_count, unsigned char *stages, Ring &R,
+                                           const GroupGemm &g) {
+    volatile int *abort = &R.abort;
+    const uint32_t idesc = idesc_bf16_f32(kBM, kBN);
+    int kstep = 0, i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait(&R.acc_empty[b], ((i / 2) - 1) & 1, g.wait_ns, abort)) {
+            R.abort = 1;
+            record_timeout(g);
+            break;
+        }
+        tc_fence_after();
+        const uint32_t acc = R.tmem_base + b * kAccCols;
+        bool ok = true;
+        for (int kb = 0; kb < kb_count; ++kb, ++kstep) {
+            const int s = kstep % kStages;
+            if (!mbar_wait(&R.full[s], (kstep / kStages) & 1, g.wait_ns, abort)) {
                 R.abort = 1;
                 record_timeout(g);
+                ok = false;
                 break;
             }
             tc_fence_after();
             const uint32_t a0 = s_addr(stages + s * kStageBytes), b0 = a0 + kATileBytes;
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)  // 16 bf16 = 32 bytes further along K
-                umma_f16(R.tmem_base, smem_desc_k_sw128(a0 + kk * 32), smem_desc_k_sw128(b0 + kk * 32), idesc,
+                umma_f16(acc, smem_desc_k_sw128(a0 + kk * 32), smem_desc_k_sw128(b0 + kk * 32), idesc,
                          (kb | kk) != 0);
             umma_commit(&R.empty[s]);
-            R.consumed = kb + 1;
+            R.consumed = kstep + 1;
         }
-        umma_commit(&R.tmem_full);  // (also after an abort: the MMAs issued so far)
+        if (!ok) break;
+        umma_commit(&R.acc_full[b]);
     }
+    umma_commit(&R.mma_done);  // every MMA issued (also after an abort)
 }
 
 // After an abort (all threads past the roles): wait, bounded, for the copies
@@ -232,9 +280,9 @@ __device__ __forceinline__ void mainloop(const CUtensorMap *map_a, const CUtenso
 __device__ __forceinline__ void drain_ring(Ring &R, const GroupGemm &g) {
     if (threadIdx.x != 0) return;
     volatile int no_abort = 0;
-    for (int kb = R.consumed; kb < R.issued; ++kb)
-        mbar_wait(&R.full[kb % kStages], (kb / kStages) & 1, g.wait_ns, &no_abort);
-    mbar_wait(&R.tmem_full, 0, g.wait_ns, &no_abort);
+    for (int k = R.consumed; k < R.issued; ++k)
+        mbar_wait(&R.full[k % kStages], (k / kStages) & 1, g.wait_ns, &no_abort);
+    mbar_wait(&R.mma_done, 0, g.wait_ns, &no_abort);
 }
 
 }  // namespace gemm
