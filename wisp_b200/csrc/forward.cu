@@ -38,8 +38,13 @@ namespace wisp {
 
 namespace {
 
-constexpr int kFwdThreads = kPagerThreads;  // 256: block 0 must run the pager
-constexpr int kWarpsPerBlock = kFwdThreads / 32;
+// Warps per block (block 0 runs the pager with all of them): 8 with three
+// copy stages each for single-token calls (the per-warp pipeline depth
+// matters most there), 12 with two stages (the same shared memory) otherwise,
+// where more warps per SM hide more of each unit's latency.
+constexpr int kWarpsDeep = 8;
+constexpr int kWarpsWide = 12;
+static_assert(kWarpsDeep * 32 >= kPagerThreads && kWarpsWide * 32 >= kPagerThreads, "the pager needs >= kPagerThreads");
 constexpr int kBlocksPerSm = 1;             // weight batches are held in registers
 constexpr int kMetaU = 256;                 // unique experts in the shared-memory lists
 constexpr int kMetaP = 256;                 // (token, k) pairs in the shared-memory lists
@@ -356,17 +361,19 @@ __device__ __forceinline__ void gu_pass(const GroupCompute &a, const Meta &m, in
     }
 }
 
-// Activation rows of up to kPairPass pairs, kept in registers across the down
-// units of one expert.
+// Activation rows of up to CP pairs, kept in registers across the down units
+// of one expert (CP 4 with 8 warps per block; 2 with 12, within their
+// register budget).
+template <int CP>
 struct ActCache {
-    uint4 v[kPairPass][kDqChunks];
+    uint4 v[CP][kDqChunks];
 };
 
 // One pass of a down unit over P pairs starting at list entry qb; `cache`
 // holds the pairs' activation rows when the expert has at most kPairPass pairs.
-template <int P, bool CACHED, int OFF = 0>
+template <int P, bool CACHED, int OFF = 0, int CP = kPairPass>
 __device__ __forceinline__ void dn_pass(const GroupCompute &a, const Meta &m, int qb, const unsigned char *st,
-                                        int h0, int nr, int lane, const ActCache &cache) {
+                                        int h0, int nr, int lane, const ActCache<CP> &cache) {
     const int H = a.H, I = a.I;
     const uint4 *ws = reinterpret_cast<const uint4 *>(st);
     float acc[4][P];
@@ -405,9 +412,9 @@ __device__ __forceinline__ void dn_pass(const GroupCompute &a, const Meta &m, in
 // kActEmpty; each element is written once per launch by one 2-byte store), poll
 // this lane's chunks of them (bounded).  With CACHED (at most kPairPass pairs)
 // the rows land in `cache`.  Returns false when the kernel is aborting.
-template <bool CACHED>
+template <bool CACHED, int CP>
 __device__ bool poll_act(const GroupCompute &a, const Meta &m, int q0, int np, int lane,
-                         const ForwardParams &fp, ActCache &cache) {
+                         const ForwardParams &fp, ActCache<CP> &cache) {
     const int I = a.I;
     unsigned long long t0 = 0;
     volatile unsigned int *vabort = fp.bar + kBarAbort;
@@ -415,7 +422,7 @@ __device__ bool poll_act(const GroupCompute &a, const Meta &m, int q0, int np, i
         bool full = true;
         if (CACHED) {
 #pragma unroll
-            for (int t = 0; t < kPairPass; ++t)
+            for (int t = 0; t < CP; ++t)
                 if (t < np)
 #pragma unroll
                     for (int c4 = 0; c4 < kDqChunks; ++c4) {
@@ -460,6 +467,7 @@ __device__ bool poll_act(const GroupCompute &a, const Meta &m, int q0, int np, i
 // Optional per-warp trace (debug; `wtr` null when off): [0] start, [1] first
 // unit's data ready, [2] gate-up items done, [3] all items done, [4] ns in
 // copy waits, [5] ns in activation polls, [6] items; %globaltimer.
+template <int CP>
 __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S, int lane,
                            const ForwardParams &fp, WarpPipe &w, bool dataflow,
                            unsigned long long *wtr = nullptr) {
@@ -532,13 +540,13 @@ __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S
     }
     if (wtr && lane == 0) wtr[2] = globaltimer_ns();
     // ---- down items
-    ActCache cache;
+    ActCache<CP> cache;
     int cache_u = -1, ready_u = -1;
     while (ok && !cmp.done) {
         const int u = S.u0 + cmp.e, h0 = 4 * cmp.r, nr = min(4, H - h0);
         const int q0 = m.off[u], q1 = m.off[u + 1], np = q1 - q0;
         const unsigned char *st = w.buf + s * kStageBytes;
-        const bool cached = np <= kPairPass;
+        const bool cached = np <= CP;
         if (dataflow && u != ready_u) {
             const unsigned long long ta = wtr ? globaltimer_ns() : 0;
             if (!(cached ? poll_act<true>(a, m, q0, np, lane, fp, cache)
@@ -552,7 +560,7 @@ __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S
         }
         if (cached && u != cache_u) {  // this expert's activation rows, reused by its next units
 #pragma unroll
-            for (int t = 0; t < kPairPass; ++t)
+            for (int t = 0; t < CP; ++t)
                 if (t < np)
 #pragma unroll
                     for (int c4 = 0; c4 < kDqChunks; ++c4) {
@@ -566,21 +574,26 @@ __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S
             break;
         }
         if (cached) {
-            if (np == 4) {
-                dn_pass<4, true>(a, m, q0, st, h0, nr, lane, cache);
+            if constexpr (CP >= 4) {
+                if (np == 4) {
+                    dn_pass<4, true, 0, CP>(a, m, q0, st, h0, nr, lane, cache);
+                } else {
+                    if (np >= 2) dn_pass<2, true, 0, CP>(a, m, q0, st, h0, nr, lane, cache);
+                    if (np == 3) dn_pass<1, true, 2, CP>(a, m, q0 + 2, st, h0, nr, lane, cache);
+                    if (np == 1) dn_pass<1, true, 0, CP>(a, m, q0, st, h0, nr, lane, cache);
+                }
             } else {
-                if (np >= 2) dn_pass<2, true>(a, m, q0, st, h0, nr, lane, cache);
-                if (np == 3) dn_pass<1, true, 2>(a, m, q0 + 2, st, h0, nr, lane, cache);
-                if (np == 1) dn_pass<1, true>(a, m, q0, st, h0, nr, lane, cache);
+                if (np == 2) dn_pass<2, true, 0, CP>(a, m, q0, st, h0, nr, lane, cache);
+                if (np == 1) dn_pass<1, true, 0, CP>(a, m, q0, st, h0, nr, lane, cache);
             }
         } else {
             int qb = q0;
-            for (; qb + 4 <= q1; qb += 4) dn_pass<4, false>(a, m, qb, st, h0, nr, lane, cache);
+            for (; qb + 4 <= q1; qb += 4) dn_pass<4, false, 0, CP>(a, m, qb, st, h0, nr, lane, cache);
             if (qb + 2 <= q1) {
-                dn_pass<2, false>(a, m, qb, st, h0, nr, lane, cache);
+                dn_pass<2, false, 0, CP>(a, m, qb, st, h0, nr, lane, cache);
                 qb += 2;
             }
-            if (qb < q1) dn_pass<1, false>(a, m, qb, st, h0, nr, lane, cache);
+            if (qb < q1) dn_pass<1, false, 0, CP>(a, m, qb, st, h0, nr, lane, cache);
         }
         __syncwarp();
         ++units;
@@ -840,16 +853,17 @@ __device__ bool block_wait_word(const unsigned int *word, unsigned int want, con
 // forms one token group no grid barrier at all (down units poll the
 // activation rows they need).  Otherwise the generic bodies with grid
 // barriers between phases.  The host picks the variant from the shapes alone.
-template <int MAXP, bool FAST>
-__global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(const __grid_constant__ ForwardParams a) {
+template <int MAXP, bool FAST, int NW>
+__global__ void __launch_bounds__(NW * 32, kBlocksPerSm) forward_kernel(const __grid_constant__ ForwardParams a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ Meta meta;
     constexpr int MAXQ = MAXP < 4 ? MAXP : 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const int nwarps = gridDim.x * kWarpsPerBlock;
-    const int gw = blockIdx.x * kWarpsPerBlock + warp;
+    const int nwarps = gridDim.x * NW;
+    const int gw = blockIdx.x * NW + warp;
     const PagerParams &pg = a.pg;
     const int H = a.gc.H, I = a.gc.I, nq = (H + 3) / 4;
+    constexpr int CP = NW > kWarpsDeep ? 2 : kPairPass;  // activation-cache pairs (register budget)
     unsigned long long *tr = a.trace;
 #define WISP_TRACE(slot)                                                                 \
     do {                                                                                 \
@@ -862,12 +876,12 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
     WISP_TRACE(0);
     WISP_TRACE0(0);
     // the next launch's activation buffer: every element "not written yet"
-    for (long i = (long)blockIdx.x * kFwdThreads + tid; i < a.act_reset_words; i += (long)gridDim.x * kFwdThreads)
+    for (long i = (long)blockIdx.x * (NW * 32) + tid; i < a.act_reset_words; i += (long)gridDim.x * (NW * 32))
         a.act_reset[i] = 0xFFFFFFFFu;
 
     // per-warp copy pipelines (FAST variant); buffers overlay the pager's shared
     // memory, which block 0 is done with before its first copy
-    __shared__ __align__(8) uint64_t s_bars[kWarpsPerBlock][kMaxStages];
+    __shared__ __align__(8) uint64_t s_bars[NW][kMaxStages];
     WarpPipe pipe{};
     if (FAST) {
         pipe.nst = a.stages;
@@ -911,9 +925,9 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
             GroupCompute gc = a.gc;
             gc.t0 = 0;
             gc.t1 = pg.T;
-            spec = make_stream(0, meta.nu, true, true, gw - kWarpsPerBlock, nwarps - kWarpsPerBlock, I, nq);
+            spec = make_stream(0, meta.nu, true, true, gw - NW, nwarps - NW, I, nq);
             // (an abort shows in the next wait)
-            run_stream(gc, meta, spec, lane, a, pipe, true, tr ? tr + kTraceWarps + gw * 16 : nullptr);
+            run_stream<CP>(gc, meta, spec, lane, a, pipe, true, tr ? tr + kTraceWarps + gw * 16 : nullptr);
         }
         // every expert of the call was resident before it: the pager will find
         // one group of hits only, so nothing is left but the speculative
@@ -954,7 +968,7 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
             gc.t1 = t1;
             load_meta(a, 0, 0, nu, t1 * K, meta);
             const Stream rest = make_stream(u_lo, nu, true, true, gw, nwarps, I, nq);
-            if (!run_stream(gc, meta, rest, lane, a, pipe, true, tr ? tr + kTraceWarps + gw * 16 + 8 : nullptr))
+            if (!run_stream<CP>(gc, meta, rest, lane, a, pipe, true, tr ? tr + kTraceWarps + gw * 16 + 8 : nullptr))
                 goto done;
             WISP_TRACE(2);
             arrive_stream(gc, spec, nu, lane);
@@ -975,7 +989,7 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
                 if (FAST) load_meta(a, g, p0, nu, (t1 - t0) * K, meta);
                 // phase 1: gate-up + SiLU-mul
                 if (FAST) {
-                    run_stream(gc, meta, make_stream(0, nu, true, false, gw, nwarps, I, nq), lane, a, pipe,
+                    run_stream<CP>(gc, meta, make_stream(0, nu, true, false, gw, nwarps, I, nq), lane, a, pipe,
                                false);
                 } else {
                     gc.u_slot = pg.u_slot + p0;
@@ -989,7 +1003,7 @@ __global__ void __launch_bounds__(kFwdThreads, kBlocksPerSm) forward_kernel(cons
                 // phase 2: down x weight, last arrival per row quad combines
                 if (FAST) {
                     const Stream dn = make_stream(0, nu, false, true, gw, nwarps, I, nq);
-                    if (run_stream(gc, meta, dn, lane, a, pipe, false)) arrive_stream(gc, dn, nu, lane);
+                    if (run_stream<CP>(gc, meta, dn, lane, a, pipe, false)) arrive_stream(gc, dn, nu, lane);
                 } else {
                     gc.u_slot = pg.u_slot + p0;
                     gc.u_off = pg.u_off + p0 + g;
@@ -1023,7 +1037,7 @@ done:
     }
 }
 
-template <int MAXP, bool FAST>
+template <int MAXP, bool FAST, int NW>
 int launch_t(const ForwardParams &p, size_t smem, cudaStream_t stream) {
     static int nblk_per_sm[64];
     static size_t smem_set[64];
@@ -1031,20 +1045,20 @@ int launch_t(const ForwardParams &p, size_t smem, cudaStream_t stream) {
     WISP_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return WISP_ERR_INVALID;
     if (smem_set[dev] < smem || !nblk_per_sm[dev]) {
-        WISP_CUDA_TRY(cudaFuncSetAttribute(forward_kernel<MAXP, FAST>,
+        WISP_CUDA_TRY(cudaFuncSetAttribute(forward_kernel<MAXP, FAST, NW>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         int nb = 0;
-        WISP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, forward_kernel<MAXP, FAST>, kFwdThreads, smem));
+        WISP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, forward_kernel<MAXP, FAST, NW>, NW * 32, smem));
         if (nb < 1) return set_error("forward kernel does not fit on an SM"), WISP_ERR_UNSUPPORTED;
         nblk_per_sm[dev] = nb > kBlocksPerSm ? kBlocksPerSm : nb;
         smem_set[dev] = smem;
     }
     int sms = 0;
     WISP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    dim3 grid(sms * nblk_per_sm[dev]), block(kFwdThreads);
+    dim3 grid(sms * nblk_per_sm[dev]), block(NW * 32);
     ForwardParams arg = p;
     void *args[] = {&arg};
-    WISP_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)forward_kernel<MAXP, FAST>, grid, block, args,
+    WISP_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)forward_kernel<MAXP, FAST, NW>, grid, block, args,
                                               smem, stream));
     return WISP_OK;
 }
@@ -1058,17 +1072,19 @@ int launch_forward(const ForwardParams &p, int max_tokens_per_group, cudaStream_
                       p.gc.I <= kDqChunks * 256 && 2L * 2 * p.gc.H <= kStageBytes &&
                       4L * 2 * p.gc.I <= kStageBytes;
     if (fast) {
-        // three stages per warp while the hidden states stay small enough for L1
-        // next to them, else two
         ForwardParams q = p;
-        q.stages = (long)p.pg.T * p.gc.H * 2 <= 16384 ? 3 : 2;
-        const size_t stages = (size_t)kWarpsPerBlock * q.stages * kStageBytes;
-        smem = smem > stages ? smem : stages;
-        return launch_t<1, true>(q, smem, stream);
+        if ((long)p.pg.T * p.pg.K <= 8) {  // one token: 8 warps x 3 stages
+            q.stages = 3;
+            const size_t st = (size_t)kWarpsDeep * 3 * kStageBytes;
+            return launch_t<1, true, kWarpsDeep>(q, smem > st ? smem : st, stream);
+        }
+        q.stages = 2;  // 12 warps x 2 stages
+        const size_t st = (size_t)kWarpsWide * 2 * kStageBytes;
+        return launch_t<1, true, kWarpsWide>(q, smem > st ? smem : st, stream);
     }
-    if (max_tokens_per_group <= 1) return launch_t<1, false>(p, smem, stream);
-    if (max_tokens_per_group <= 4) return launch_t<4, false>(p, smem, stream);
-    return launch_t<8, false>(p, smem, stream);
+    if (max_tokens_per_group <= 1) return launch_t<1, false, kWarpsDeep>(p, smem, stream);
+    if (max_tokens_per_group <= 4) return launch_t<4, false, kWarpsDeep>(p, smem, stream);
+    return launch_t<8, false, kWarpsDeep>(p, smem, stream);
 }
 
 }  // namespace wisp

@@ -161,32 +161,34 @@ static __device__ __forceinline__ int pager_id(const PagerParams &a, const Smem 
     return S.ids ? S.ids[p] : (int)load_id64(a.ids, a.ids64, p);
 }
 
-// All kThreads threads of one CTA.  On return the new state is in shared
-// memory (smem_raw) and the compute outputs are in device memory.
+// All threads of one CTA (any multiple of 32, at least kThreads).  On return
+// the new state is in shared memory (smem_raw) and the compute outputs are in
+// device memory.
 static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned char *smem_raw) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nth = blockDim.x;
     const int E = a.E, cap = a.cap, K = a.K, T = a.T;
     const Smem S = carve(smem_raw, E, cap, T, K, a.grp_start);
     Scalars &sc = *S.sc;
     int *mb_miss = a.mb + mailbox_miss_offset(T);
 
     // ---- load state and ids ---------------------------------------------------
-    for (int s = tid; s < cap; s += kThreads) {
+    for (int s = tid; s < cap; s += nth) {
         S.tick[s] = a.tick[s];
         S.s2e[s] = a.s2e[s];
         S.lastg[s] = -1;
         S.fresh[s] = 0;
     }
-    for (int e = tid; e < E; e += kThreads) S.emap[e] = a.emap[e];
+    for (int e = tid; e < E; e += nth) S.emap[e] = a.emap[e];
     int bad = 0;
     if (S.ids) {
-        for (long p = tid; p < (long)T * K; p += kThreads) {
+        for (long p = tid; p < (long)T * K; p += nth) {
             const long long e = load_id64(a.ids, a.ids64, p);
             bad |= (e < 0 || e >= E);
             S.ids[p] = (int)e;
         }
     } else {
-        for (long p = tid; p < (long)T * K; p += kThreads) {
+        for (long p = tid; p < (long)T * K; p += nth) {
             const long long e = load_id64(a.ids, a.ids64, p);
             bad |= (e < 0 || e >= E);
         }
@@ -250,7 +252,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
         const long p0 = (long)t0 * K, p1 = (long)t1 * K;
         if (tid < kMaxMaskWords) sc.mask[tid] = 0;
         __syncthreads();
-        for (long p = p0 + tid; p < p1; p += kThreads) {
+        for (long p = p0 + tid; p < p1; p += nth) {
             const int e = pager_id(a, S, p);
             atomicOr(&sc.mask[e >> 5], 1u << (e & 31));
         }
@@ -339,7 +341,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
                 const int nfree = sc.nfree, need = sc.need;
                 if (need > 0) {
                     // rank each candidate by (tick, slot); the first `need` are victims
-                    for (int s = tid; s < cap; s += kThreads) {
+                    for (int s = tid; s < cap; s += nth) {
                         const int e = S.s2e[s];
                         if (e < 0 || ((sc.mask[e >> 5] >> (e & 31)) & 1u)) continue;
                         const long long ts = S.tick[s];
@@ -353,7 +355,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
                         if (rank < need) S.fre[nfree + rank] = s;
                     }
                     __syncthreads();
-                    for (int r = tid; r < need; r += kThreads) {
+                    for (int r = tid; r < need; r += nth) {
                         const int s = S.fre[nfree + r];
                         S.emap[S.s2e[s]] = -1;
                         S.s2e[s] = -1;
@@ -366,7 +368,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
                 __syncthreads();
                 const long long clk = sc.clock;
                 const int mbase = sc.mtotal;
-                for (int i = tid; i < nm; i += kThreads) {
+                for (int i = tid; i < nm; i += nth) {
                     const int e = S.miss[i];
                     const int s = S.fre[total_free - 1 - i];  // LIFO pop
                     S.emap[e] = s;
@@ -392,7 +394,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
                 __syncthreads();
             }
             const long long clk = sc.clock;
-            for (int i = tid; i < n; i += kThreads) {
+            for (int i = tid; i < n; i += nth) {
                 const int s = S.emap[S.asc[i]];
                 S.tick[s] = clk;
                 S.lastg[s] = g;
@@ -416,10 +418,10 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
             if (lane == 0) sc.nhit = nh;
         }
         __syncthreads();
-        for (int i = tid; i < nm; i += kThreads) S.uord[sc.nhit + i] = S.miss[i];
+        for (int i = tid; i < nm; i += nth) S.uord[sc.nhit + i] = S.miss[i];
         __syncthreads();
         // per-(t,k) slots and per-group unique-slot CSR for the compute kernels
-        for (int i = tid; i < n; i += kThreads) {
+        for (int i = tid; i < n; i += nth) {
             const int e = S.uord[i];
             S.pos[e] = i;
             S.cnt[i] = 0;
@@ -431,7 +433,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
             a.u_gen[p0 + i] = S.fresh[s] ? (int)a.slot_gen[s] : 0;
         }
         __syncthreads();
-        for (long p = p0 + tid; p < p1; p += kThreads) {
+        for (long p = p0 + tid; p < p1; p += nth) {
             const int e = pager_id(a, S, p);
             a.slots[p] = S.emap[e];
             atomicAdd(&S.cnt[S.pos[e]], 1);
@@ -457,7 +459,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
             if (lane == 0) a.u_off[p0 + g + n] = run;
         }
         __syncthreads();
-        for (long p = p0 + tid; p < p1; p += kThreads) {
+        for (long p = p0 + tid; p < p1; p += nth) {
             const int i = S.pos[pager_id(a, S, p)];
             const int at = atomicAdd(&S.fill[i], 1);
             a.u_pairs[p0 + S.cnt[i] + at] = (int)p;
@@ -478,7 +480,7 @@ finish:
         a.dev_hdr[kHdrUnique] = sc.utotal;
     }
     if (S.grp != a.grp_start)
-        for (int g = tid; g <= sc.G; g += kThreads) a.grp_start[g] = S.grp[g];
+        for (int g = tid; g <= sc.G; g += nth) a.grp_start[g] = S.grp[g];
     __threadfence();  // every thread's outputs visible device-wide before the CTA moves on
     __syncthreads();
 }
@@ -487,16 +489,16 @@ finish:
 // state back and publish the groups and the page-in list to the mailbox.
 static __device__ __noinline__ void pager_finish(const PagerParams &a, unsigned char *smem_raw,
                                                  bool publish) {
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, nth = blockDim.x;
     const int E = a.E, cap = a.cap, T = a.T;
     const Smem S = carve(smem_raw, E, cap, T, a.K, a.grp_start);
     const Scalars &sc = *S.sc;
     if (sc.status == WISP_OK || sc.status == WISP_ERR_OVERFLOW) {
-        for (int s = tid; s < cap; s += kThreads) {
+        for (int s = tid; s < cap; s += nth) {
             a.tick[s] = S.tick[s];
             a.s2e[s] = S.s2e[s];
         }
-        for (int e = tid; e < E; e += kThreads) a.emap[e] = S.emap[e];
+        for (int e = tid; e < E; e += nth) a.emap[e] = S.emap[e];
         if (tid == 0) {
             a.hdr[0] = sc.clock;
             for (int i = 0; i < 4; ++i) a.hdr[1 + i] = sc.stat[i];
@@ -508,8 +510,8 @@ static __device__ __noinline__ void pager_finish(const PagerParams &a, unsigned 
         int *mb_grp = a.mb + kMbHeader;
         int *mb_nu = mb_grp + (T + 1);
         const int G = sc.status == WISP_OK ? sc.G : 0;
-        for (int g = tid; g <= G; g += kThreads) mb_grp[g] = S.grp[g];
-        for (int g = tid; g < G; g += kThreads) mb_nu[g] = a.grp_nu[g];
+        for (int g = tid; g <= G; g += nth) mb_grp[g] = S.grp[g];
+        for (int g = tid; g < G; g += nth) mb_nu[g] = a.grp_nu[g];
         __syncthreads();
         if (tid == 0) {
             a.mb[1] = sc.G;
