@@ -477,7 +477,10 @@ def run_wisp_ep(args):
     total = args.warmup + args.steps
     t0 = time.time()
     masters = make_shard_masters(L, dev, rank, world)
-    layers = [EPMoELayer(h13, h2, E, C, "paged", dev, i) for i, (h13, h2) in enumerate(masters)]
+    # a cap that holds the whole shard makes it resident (primed once; the
+    # one-launch forward), otherwise the shard pages
+    mode = "resident" if C == per else "paged"
+    layers = [EPMoELayer(h13, h2, E, C, mode, dev, i) for i, (h13, h2) in enumerate(masters)]
     ids_all, w_all = routing(total, L, B * world)
     ids_d = torch.from_numpy(np.ascontiguousarray(ids_all[:, :, rank * B:(rank + 1) * B])).to(dev)
     w_d = torch.from_numpy(np.ascontiguousarray(w_all[:, :, rank * B:(rank + 1) * B])).to(dev)
@@ -560,7 +563,8 @@ def run_wisp_ep(args):
         "config": {"workload": f"qwen3-30b-a3b {L}-layer expert stack, expert-parallel over {world} GPUs, "
                                f"decode batch {B} per GPU, cap {C} per GPU",
                    "layers": L, "batch_per_gpu": B, "global_batch": B * world, "cap_per_gpu": C,
-                   "experts_per_gpu": per, "parallelism": f"ep{world}", "routing": "zipf1.1 reuse0.6",
+                   "experts_per_gpu": per, "shard_mode": mode, "parallelism": f"ep{world}",
+                   "routing": "zipf1.1 reuse0.6",
                    "l2": "inputs larger than L2 (each step reads every layer's routed experts from HBM)"},
         "gpu_launches": int(stats[2]),
         "roofline": None,

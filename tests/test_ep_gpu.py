@@ -72,8 +72,6 @@ def test_ep_emulated_ranks_match_one_gpu(P, cap, mode):
         lo, hi = shard_range(E, r, P)
         layers.append(EPMoELayer(w13[lo:hi], w2[lo:hi], E, cap, mode, DEV, 0, rank=r, world_size=P))
         oracles.append(PagerOracle(E // P, cap))
-        if mode == "resident":
-            layers[r].local.prime_identity()
     full = WispMoEState(w13, w2, E, "resident", DEV, 0)
     full.prime_identity()
     for step in range(4):

@@ -72,6 +72,8 @@ class EPMoELayer:
                 raise ValueError(f"rank {self.rank} shard has {cpu_w13_shard.shape[0]} experts, "
                                  f"expected {self.experts_per_rank}")
             local = WispMoEState(cpu_w13_shard, cpu_w2_shard, cap_experts, mode, device, layer_idx)
+            if mode == "resident":  # the whole shard in HBM (cap == experts per rank)
+                local.prime_identity()
         self.local = local
         self.device = torch.device(device) if device is not None else getattr(local, "device", None)
         self.hidden = int(getattr(local, "hidden_size", 0))
