@@ -154,13 +154,19 @@ WISP_API int wisp_layer_sync(wisp_layer *layer);
  * host silently skips the next n page-ins of this layer),
  * WISP_CFG_TRACE_BUFFER (debug: device address of a uint64 buffer of
  * 8 + 4 * grid words that the forward kernel fills with %globaltimer
- * milestones; 0 = off).
+ * milestones; 0 = off), WISP_CFG_TC_MIN_PAIRS (calls of at least this many
+ * (token, k) pairs run their expert compute on the tcgen05 tensor cores --
+ * weight-stationary tiles up to 256 pairs, token-major GEMMs above -- where
+ * hidden % 256 == 0 and inter % 128 == 0; smaller calls on the CUDA-core
+ * decode kernels.  The choice depends on the call size only, so outputs stay
+ * byte-identical across caps and modes; default 64, capped at 257).
  */
 enum wisp_config_key {
     WISP_CFG_ASYNC = 1,
     WISP_CFG_WAIT_NS = 2,
     WISP_CFG_DROP_PAGEINS = 4,
-    WISP_CFG_TRACE_BUFFER = 5
+    WISP_CFG_TRACE_BUFFER = 5,
+    WISP_CFG_TC_MIN_PAIRS = 6
 };
 WISP_API int wisp_layer_config(wisp_layer *layer, int32_t key, int64_t value);
 

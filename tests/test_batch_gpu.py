@@ -1,0 +1,141 @@
+"""Decode batches on the weight-stationary tensor-core path (calls of
+tc_min_pairs <= T * k <= 256 pairs): parity with the fp32 CPU oracle under
+the same bounds as the prefill path (mean-rel <= 1e-3; per element
+|out - ref| <= max(1e-2, 2 ulp(ref) + sum over k of 2 ulp(y_k)), the stored
+bf16 values may each round the other way with another fp32 accumulation
+order), byte identity across caps, modes and slot placements, agreement with
+the token-major GEMMs on the same pairs, the pager state unchanged by the
+path, the kernel count (resident: pager + gather, fused gate-up/down,
+combine, with no host round trip; paged: pager + 3 per group), the threshold
+knob, and a routed id out of range reported at synchronize."""
+import pytest
+import torch
+
+from oracle.moe import compare, moe_reference
+from oracle.pager import PagerOracle, forward_pager
+from tests.test_moe_gpu import MAX_ABS, MEAN_REL, fwd, rand_case, state
+from wisp_b200 import _lib
+from wisp_b200 import workloads as wl
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def _bf16_ulp(v):
+    return torch.ldexp(torch.ones_like(v), torch.frexp(v.abs().clamp_min(1e-30))[1] - 8)
+
+
+def assert_parity(out, x, w13, w2, w, ids):
+    ref, Y = moe_reference(x, w13, w2, w, ids, return_partials=True)
+    c = compare(out, ref)
+    assert c["mean_rel"] <= MEAN_REL, c
+    bound = torch.clamp_min(2 * _bf16_ulp(ref) + (2 * _bf16_ulp(Y)).sum(dim=1), MAX_ABS)
+    d = (out.float() - ref).abs()
+    assert bool((d <= bound).all()), (c, float((d - bound).max()))
+    return c
+
+
+@pytest.mark.parametrize("E,H,I,T,K,cap,mode", [
+    (128, 2048, 768, 16, 8, 128, "resident"),   # Qwen3-30B-A3B decode, batch 16
+    (128, 2048, 768, 8, 8, 128, "resident"),    # batch 8 (64 pairs: the default threshold)
+    (128, 2048, 768, 16, 8, 40, "paged"),       # paged, several groups
+    (8, 4096, 1536, 32, 2, 8, "resident"),      # Qwen3-235B hidden/inter, top-2, 8 tokens/expert
+    (16, 256, 128, 64, 4, 16, "resident"),      # small shapes, > 32 pairs per expert (several token blocks)
+    (32, 512, 256, 40, 4, 12, "paged"),
+])
+def test_batch_matches_oracle(E, H, I, T, K, cap, mode):
+    w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=T * K + H)
+    st = state(w13, w2, cap, mode)
+    out = fwd(st, x, w, ids)
+    assert_parity(out, x, w13, w2, w, ids)
+    assert torch.equal(fwd(st, x, w, ids), out)
+    st.close()
+
+
+def test_batch_byte_identical_across_caps_modes_and_placements():
+    E, H, I, T, K = 32, 512, 256, 24, 4
+    w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=17)
+    outs = []
+    for cap, mode in ((32, "resident"), (32, "paged"), (20, "paged"), (9, "paged")):
+        st = state(w13, w2, cap, mode)
+        if mode == "paged":  # a different slot placement first
+            st.ensure_resident(torch.arange(E - 1, E - 1 - min(cap, E), -1, dtype=torch.int32))
+        outs.append(fwd(st, x, w, ids))
+        st.close()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+
+
+def test_batch_agrees_with_token_major_gemm():
+    """256 pairs run weight-stationary, 264 pairs token-major: the first 32
+    tokens' outputs (the same pairs) are byte-identical, so the two
+    tensor-core paths are one numeric class."""
+    E, H, I, K = 32, 512, 256, 8
+    w13, w2, x, w, ids = rand_case(E, H, I, 33, K, seed=23)
+    st = state(w13, w2, E, "resident")
+    big = fwd(st, x, w, ids)                    # 264 pairs: token-major GEMMs
+    small = fwd(st, x[:32], w[:32], ids[:32])   # 256 pairs: weight-stationary
+    assert torch.equal(big[:32], small)
+    st.close()
+
+
+def test_batch_pager_state_and_kernel_count():
+    E, H, I, T, K, cap = 32, 256, 128, 20, 4, 10
+    w13, w2, x, _, _ = rand_case(E, H, I, T, K, seed=29)
+    st = state(w13, w2, cap)
+    oracle = PagerOracle(E, cap)
+    for step in range(3):
+        g = torch.Generator().manual_seed(200 + step)
+        w, ids = wl.softmax_topk(torch.randn(T, E, generator=g), K)
+        l0, g0 = st.telemetry()["kernel_launches"], st.telemetry()["groups"]
+        out = fwd(st, x, w, ids)
+        groups, _, _ = forward_pager(oracle, ids.numpy())
+        tel = st.telemetry()
+        assert tel["groups"] - g0 == len(groups)
+        assert tel["kernel_launches"] - l0 == 1 + 3 * len(groups)
+        s2e, tick, clock, stats = st._read()
+        assert s2e == oracle.slot_to_expert and tick == oracle.lru_tick and clock == oracle.lru_clock
+        assert stats == oracle.stats()
+        assert_parity(out, x, w13, w2, w, ids)
+    st.close()
+    res = state(w13, w2, E, "resident")
+    l0 = res.telemetry()["kernel_launches"]
+    res.forward(x.to(DEV), w.to(DEV), ids.to(DEV))
+    res.synchronize()
+    assert res.telemetry()["kernel_launches"] - l0 == 4
+    assert res.stats()[0] == 1
+    res.close()
+
+
+def test_threshold_knob_selects_the_path():
+    E, H, I, T, K = 16, 256, 128, 8, 4   # 32 pairs: CUDA-core kernels by default
+    w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=31)
+    st = state(w13, w2, E, "resident")
+    l0 = st.telemetry()["kernel_launches"]
+    a = fwd(st, x, w, ids)
+    assert st.telemetry()["kernel_launches"] - l0 == 1      # one-launch forward
+    st.configure(tc_min_pairs=32)
+    l0 = st.telemetry()["kernel_launches"]
+    b = fwd(st, x, w, ids)
+    assert st.telemetry()["kernel_launches"] - l0 == 4      # pager + 3
+    for o in (a, b):
+        assert_parity(o, x, w13, w2, w, ids)
+    with pytest.raises(_lib.WispError):
+        st.configure(tc_min_pairs=0)
+    st.close()
+
+
+def test_batch_bad_expert_reported_at_sync_then_recovers():
+    E, H, I, T, K = 16, 256, 128, 16, 4
+    w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=37)
+    st = state(w13, w2, E, "resident")
+    bad = ids.clone()
+    bad[3, 1] = E + 5
+    st.forward(x.to(DEV), w.to(DEV), bad.to(torch.int32).to(DEV))
+    with pytest.raises(_lib.WispError) as ei:
+        st.synchronize()
+    assert ei.value.code == _lib.WISP_ERR_BAD_EXPERT
+    assert st.stats()[0] == 0                               # rejected before any bookkeeping
+    out = fwd(st, x, w, ids)
+    assert_parity(out, x, w13, w2, w, ids)
+    st.close()

@@ -27,6 +27,7 @@ CFG_ASYNC = 1
 CFG_WAIT_NS = 2
 CFG_DROP_PAGEINS = 4
 CFG_TRACE_BUFFER = 5
+CFG_TC_MIN_PAIRS = 6
 
 _c_int32 = ctypes.c_int32
 _c_int64 = ctypes.c_int64

@@ -15,8 +15,21 @@ __device__ __forceinline__ unsigned char *align1024(unsigned char *p) {
     return p + ((1024u - (a & 1023u)) & 1023u);
 }
 
-// X_perm[q] = x[token of pair q]: one warp per row, 16-byte copies.
-__global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int K, int H8, uint4 *xp) {
+// X_perm[q] = x[token of pair q]: one warp per row, 16-byte copies.  Also
+// zeroes the weight-stationary path's per-block counters (`ready`).  When the
+// pager ran without a host check and rejected the call, the lists are stale:
+// nothing is read and block 0 records the pager's status in the sticky word.
+__global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int K, int H8, uint4 *xp,
+                              uint32_t *ready, int nready, const int32_t *pager_status, int *status) {
+    if (pager_status) {
+        const int st = *reinterpret_cast<const volatile int32_t *>(pager_status);
+        if (st != WISP_OK) {
+            if (blockIdx.x == 0 && threadIdx.x == 0 && status) *reinterpret_cast<volatile int *>(status) = st;
+            return;
+        }
+    }
+    if (ready)
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nready; i += gridDim.x * blockDim.x) ready[i] = 0;
     const int q = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (q >= P) return;
     const uint4 *src = x + (size_t)(u_pairs[q] / K) * H8;
@@ -52,7 +65,7 @@ __device__ __forceinline__ void tile_of(const TileTable &tt, int m, int &u, int 
 // accumulators).  Returns the number of tiles (n_cols tiles per m tile); a CTA
 // with none returns 0 before allocating anything.
 __device__ __forceinline__ int gemm_setup(const GroupGemm &g, int n_cols, TileTable &tt, Ring &R) {
-    const int nu = min(g.nu, kMaxTileExperts);
+    const int nu = min(group_experts(g.nu_dev, g.pager_status), kMaxTileExperts);
     for (int i = threadIdx.x; i <= nu; i += blockDim.x) tt.off[i] = g.u_off[i];
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -234,7 +247,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // out[t] = sum over k in routing order of y[t * K + k], t in [t0, t1).
-__global__ void combine_kernel(const uint4 *y, int t0, int t1, int K, int H8, uint4 *out) {
+__global__ void combine_kernel(const uint4 *y, int t0, int t1, int K, int H8, uint4 *out,
+                               const int32_t *pager_status) {
+    if (pager_status && *reinterpret_cast<const volatile int32_t *>(pager_status) != WISP_OK) return;
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long)(t1 - t0) * H8) return;
     const int t = t0 + (int)(i / H8), c = (int)(i % H8);
@@ -275,14 +290,14 @@ void init_encode() {
         cudaGetLastError();
 }
 
-// Row-major bf16 matrix [rows][cols] (16-byte aligned base, cols % 8 == 0) as
-// 64 x 128 boxes with 128-byte swizzle.
-int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols) {
+}  // namespace
+
+int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
     std::call_once(g_encode_once, init_encode);
     if (!g_encode) return set_error("wisp: cuTensorMapEncodeTiled is not available"), WISP_ERR_UNSUPPORTED;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kHalfN};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -291,7 +306,27 @@ int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols) {
     return WISP_OK;
 }
 
-}  // namespace
+int launch_gather(const PrefillGroup &p, uint32_t *ready, int nready, cudaStream_t stream) {
+    const int warps = 8;
+    const int blocks = std::max((p.npairs + warps - 1) / warps, ready ? (nready + warps * 32 - 1) / (warps * 32) : 0);
+    if (blocks <= 0) return WISP_OK;
+    gather_kernel<<<blocks, warps * 32, 0, stream>>>(reinterpret_cast<const uint4 *>(p.x), p.u_pairs, p.npairs, p.K,
+                                                     p.H / 8, reinterpret_cast<uint4 *>(p.x_perm), ready, nready,
+                                                     p.pager_status, p.status);
+    WISP_CUDA_TRY(cudaGetLastError());
+    return WISP_OK;
+}
+
+int launch_combine(const PrefillGroup &p, cudaStream_t stream) {
+    const long n = (long)(p.t1 - p.t0) * (p.H / 8);
+    if (n <= 0) return WISP_OK;
+    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const uint4 *>(p.y), p.t0, p.t1, p.K, p.H / 8, reinterpret_cast<uint4 *>(p.out),
+        p.pager_status);
+    WISP_CUDA_TRY(cudaGetLastError());
+    return WISP_OK;
+}
+
 }  // namespace gemm
 
 bool prefill_shapes_supported(int H, int I) {
@@ -313,16 +348,17 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
         attr_set[dev] = true;
     }
     CUtensorMap mx, mw13, mact, mw2;
-    int rc = make_map(&mx, p.x_perm, (uint64_t)p.perm_rows, (uint64_t)p.H);
-    if (!rc) rc = make_map(&mw13, p.w13, (uint64_t)p.slots * 2 * p.I, (uint64_t)p.H);
-    if (!rc) rc = make_map(&mact, p.act_perm, (uint64_t)p.perm_rows, (uint64_t)p.I);
-    if (!rc) rc = make_map(&mw2, p.w2, (uint64_t)p.slots * p.H, (uint64_t)p.I);
+    int rc = make_map(&mx, p.x_perm, (uint64_t)p.perm_rows, (uint64_t)p.H, kHalfN);
+    if (!rc) rc = make_map(&mw13, p.w13, (uint64_t)p.slots * 2 * p.I, (uint64_t)p.H, kHalfN);
+    if (!rc) rc = make_map(&mact, p.act_perm, (uint64_t)p.perm_rows, (uint64_t)p.I, kHalfN);
+    if (!rc) rc = make_map(&mw2, p.w2, (uint64_t)p.slots * p.H, (uint64_t)p.I, kHalfN);
     if (rc) return rc;
     GroupGemm g{};
     g.u_off = p.u_off;
     g.u_pairs = p.u_pairs;
     g.u_slot = p.u_slot;
-    g.nu = p.nu;
+    g.nu_dev = p.nu_dev;
+    g.pager_status = p.pager_status;
     g.H = p.H;
     g.I = p.I;
     g.K = p.K;
@@ -332,28 +368,19 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
     g.status = p.status;
     g.wait_ns = p.wait_ns;
     // persistent grids: at most one CTA per SM (tiles: at most one partial
-    // 128-pair tile per expert beyond the full ones)
+    // 128-pair tile per expert beyond the full ones; `nu` bounds the count)
     int sms = 0;
     WISP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const long mtiles = (long)p.nu + (p.npairs + kBM - 1) / kBM;
     const int grid_gu = (int)std::min<long>(mtiles * (p.I / kHalfN), sms);
     const int grid_dn = (int)std::min<long>(mtiles * (p.H / kBN), sms);
-    const int warps = 8;
-    gather_kernel<<<(p.npairs + warps - 1) / warps, warps * 32, 0, stream>>>(
-        reinterpret_cast<const uint4 *>(p.x), p.u_pairs, p.npairs, p.K, p.H / 8, reinterpret_cast<uint4 *>(p.x_perm));
-    WISP_CUDA_TRY(cudaGetLastError());
+    rc = launch_gather(p, nullptr, 0, stream);
+    if (rc) return rc;
     gateup_gemm_kernel<<<grid_gu, kThreads, kSmemBytes, stream>>>(mx, mw13, g);
     WISP_CUDA_TRY(cudaGetLastError());
     down_gemm_kernel<<<grid_dn, kThreads, kSmemBytes, stream>>>(mact, mw2, g);
     WISP_CUDA_TRY(cudaGetLastError());
-    const long n = (long)(p.t1 - p.t0) * (p.H / 8);
-    if (n > 0) {
-        combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(reinterpret_cast<const uint4 *>(p.y), p.t0,
-                                                                        p.t1, p.K, p.H / 8,
-                                                                        reinterpret_cast<uint4 *>(p.out));
-        WISP_CUDA_TRY(cudaGetLastError());
-    }
-    return WISP_OK;
+    return launch_combine(p, stream);
 }
 
 }  // namespace wisp

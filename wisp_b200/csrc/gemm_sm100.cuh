@@ -43,6 +43,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "prefill.cuh"
 
 namespace wisp {
 namespace gemm {
@@ -66,7 +67,8 @@ struct GroupGemm {
     const int32_t *u_off;    // [nu + 1] pair-list offsets of the group's experts
     const int32_t *u_pairs;  // [P_g] absolute pair index (t * K + k), expert-major
     const int32_t *u_slot;   // [nu] slot of each expert
-    int nu;                  // experts in the group
+    const int32_t *nu_dev;   // experts in the group (device word written by the pager)
+    const int32_t *pager_status;  // the pager's status word (nullptr: checked by the host)
     int H, I, K;             // hidden, intermediate, top-k
     const float *topk_w;     // [T * K] routing weights (absolute pair index)
     __nv_bfloat16 *act_perm; // [P_g][I] (gate-up output, down input)
@@ -284,6 +286,22 @@ __device__ __forceinline__ void drain_ring(Ring &R, const GroupGemm &g) {
         mbar_wait(&R.full[k % kStages], (k / kStages) & 1, g.wait_ns, &no_abort);
     mbar_wait(&R.mma_done, 0, g.wait_ns, &no_abort);
 }
+
+// Experts of the group as the kernels see them: the pager's count, or none
+// when the pager (run on the device without a host check) rejected the call.
+__device__ __forceinline__ int group_experts(const int32_t *nu_dev, const int32_t *pager_status) {
+    if (pager_status && *reinterpret_cast<const volatile int32_t *>(pager_status) != WISP_OK) return 0;
+    return *reinterpret_cast<const volatile int32_t *>(nu_dev);
+}
+
+// ---- host helpers shared by the token-major and weight-stationary paths ------------
+// Row-major bf16 matrix [rows][cols] (16-byte aligned base, cols % 8 == 0) as
+// 64 x box_rows boxes with 128-byte swizzle.
+int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+// X_perm rows of the group (and, when `ready` is set, zero `nready` words of it).
+int launch_gather(const PrefillGroup &p, uint32_t *ready, int nready, cudaStream_t stream);
+// out rows [t0, t1) = routing-order sum of the weighted rows y.
+int launch_combine(const PrefillGroup &p, cudaStream_t stream);
 
 }  // namespace gemm
 }  // namespace wisp

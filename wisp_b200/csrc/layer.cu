@@ -88,6 +88,11 @@ void init_write32() {
 }
 
 constexpr long long kDefaultWaitNs = 10LL * 1000 * 1000 * 1000;
+// Calls of T * k pairs in [kDefaultTcMinPairs, kPrefillMinPairs) run on the
+// weight-stationary tensor-core path, larger ones on the token-major GEMMs,
+// smaller ones on the CUDA-core decode kernels.
+constexpr int kDefaultTcMinPairs = 64;
+constexpr int kPrefillMinPairs = 257;
 constexpr int kMbRing = 4;
 
 }  // namespace
@@ -114,7 +119,9 @@ struct wisp_layer {
             *d_u_slot = nullptr, *d_u_gen = nullptr, *d_u_off = nullptr, *d_u_pairs = nullptr,
             *d_counters = nullptr, *d_dev_hdr = nullptr;
     __nv_bfloat16 *d_act = nullptr, *d_y = nullptr;
-    __nv_bfloat16 *d_xperm = nullptr, *d_actperm = nullptr;  // prefill GEMM rows, expert-major
+    __nv_bfloat16 *d_xperm = nullptr, *d_actperm = nullptr;  // tensor-core paths: rows, expert-major
+    uint32_t *d_ready = nullptr;     // weight-stationary path: per-token-block counters
+    int tc_min_pairs = kDefaultTcMinPairs;  // calls of at least this many pairs run on the tensor cores
     int32_t *h_mb = nullptr, *d_mb = nullptr;  // kMbRing mailboxes of mb_words words
     long mb_words = 0;
     int mb_next = 0;
@@ -322,12 +329,13 @@ void free_ws(wisp_layer *L) {
                     (void *)L->d_grp_nhit, (void *)L->d_u_slot,
                     (void *)L->d_u_gen, (void *)L->d_u_off, (void *)L->d_u_pairs, (void *)L->d_counters,
                     (void *)L->d_dev_hdr, (void *)L->d_act, (void *)L->d_y, (void *)L->d_xperm,
-                    (void *)L->d_actperm})
+                    (void *)L->d_actperm, (void *)L->d_ready})
         cudaFree(p);
     if (L->h_mb) cudaFreeHost(L->h_mb);
     L->d_slots = L->d_grp_start = L->d_grp_nu = L->d_grp_nhit = L->d_u_slot = L->d_u_gen = L->d_u_off =
         L->d_u_pairs = L->d_counters = L->d_dev_hdr = nullptr;
     L->d_act = L->d_y = L->d_xperm = L->d_actperm = nullptr;
+    L->d_ready = nullptr;
     L->h_mb = L->d_mb = nullptr;
     L->wsT = -1;
     L->wsK = 0;
@@ -367,6 +375,7 @@ int ensure_ws(wisp_layer *L, int T, int K) {
         if (prefill_shapes_supported(L->H, L->I)) {
             WISP_CUDA_TRY(cudaMalloc(&L->d_xperm, sizeof(__nv_bfloat16) * P * H));
             WISP_CUDA_TRY(cudaMalloc(&L->d_actperm, sizeof(__nv_bfloat16) * P * I));
+            WISP_CUDA_TRY(cudaMalloc(&L->d_ready, sizeof(uint32_t) * batch_ready_words((long)P, (long)P)));
         }
     }
     const long words = (mailbox_words(nT, nK) + 31) & ~31L;
@@ -519,13 +528,60 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
     return WISP_OK;
 }
 
-// Calls above the decode kernels' range (T * k > 256) run their expert
-// compute as tensor-core grouped GEMMs where the shapes allow.  The choice
-// depends on the call's size only (not on its grouping), so outputs stay
-// byte-identical across caps and slot placements.
-constexpr int kPrefillMinPairs = 257;
-bool use_prefill_gemm(const wisp_layer *L, int T, int K) {
-    return (long)T * K >= kPrefillMinPairs && prefill_shapes_supported(L->H, L->I) && L->d_xperm;
+// Which kernels run a call's expert compute.  The choice depends on the
+// call's size (T * k) only, not on its grouping, so outputs stay
+// byte-identical across caps, modes and slot placements.
+enum class Path { kDecode, kBatchTC, kPrefillTC };
+Path compute_path(const wisp_layer *L, int T, int K) {
+    const long pairs = (long)T * K;
+    if (!prefill_shapes_supported(L->H, L->I)) return Path::kDecode;
+    if (pairs >= kPrefillMinPairs) return Path::kPrefillTC;
+    if (pairs >= L->tc_min_pairs) return Path::kBatchTC;
+    return Path::kDecode;
+}
+
+// A group of the call for the tensor-core launchers.
+PrefillGroup tc_group(const wisp_layer *L, const void *x, const float *w, void *out, int g, int t0, int t1,
+                      int K, int nu_bound, const int32_t *pager_status) {
+    const int64_t p0 = (int64_t)t0 * K;
+    PrefillGroup pg{};
+    pg.x = reinterpret_cast<const __nv_bfloat16 *>(x);
+    pg.w13 = reinterpret_cast<const __nv_bfloat16 *>(L->d13);
+    pg.w2 = reinterpret_cast<const __nv_bfloat16 *>(L->d2);
+    pg.slots = L->cap;
+    pg.u_off = L->d_u_off + p0 + g;
+    pg.u_pairs = L->d_u_pairs + p0;
+    pg.u_slot = L->d_u_slot + p0;
+    pg.nu_dev = L->d_grp_nu + g;
+    pg.pager_status = pager_status;
+    pg.nu = nu_bound;
+    pg.npairs = (t1 - t0) * K;
+    pg.t0 = t0;
+    pg.t1 = t1;
+    pg.K = K;
+    pg.H = L->H;
+    pg.I = L->I;
+    pg.topk_w = w;
+    pg.x_perm = L->d_xperm;
+    pg.act_perm = L->d_actperm;
+    pg.perm_rows = L->wsT * L->wsK;
+    pg.y = L->d_y;
+    pg.out = reinterpret_cast<__nv_bfloat16 *>(out);
+    pg.status = L->d_status;
+    pg.wait_ns = L->wait_ns;
+    pg.ready = L->d_ready;
+    return pg;
+}
+
+int launch_tc_group(wisp_layer *L, Path path, const PrefillGroup &pg, cudaStream_t stream) {
+    if (path == Path::kBatchTC) {
+        const int rc = launch_batch_group(pg, stream);
+        if (!rc) L->launches += kBatchKernelsPerGroup;
+        return rc;
+    }
+    const int rc = launch_prefill_group(pg, stream);
+    if (!rc) L->launches += kPrefillKernelsPerGroup;
+    return rc;
 }
 
 // Synchronous path after run_pager: page-ins per group (write-after-read via
@@ -539,6 +595,7 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
     const int32_t *rec = mb + mailbox_miss_offset(T);
     int rc = ensure_events(L, std::max(G, 1));
     if (rc) return rc;
+    const Path path = compute_path(L, T, K);
     int mi = 0;
     for (int g = 0; g < G; ++g) {
         const int t0 = grp[g], t1 = grp[g + 1];
@@ -556,35 +613,10 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
             WISP_CUDA_TRY(cudaEventRecord(L->ev_copy[g], L->copy_stream));
             WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copy[g], 0));
         }
-        if (compute && t1 > t0 && nu[g] > 0 && use_prefill_gemm(L, T, K)) {
-            // tensor-core grouped GEMMs (gather, gate-up + SiLU-mul, down, combine)
-            const int64_t p0 = (int64_t)t0 * K;
-            PrefillGroup pg{};
-            pg.x = reinterpret_cast<const __nv_bfloat16 *>(x);
-            pg.w13 = reinterpret_cast<const __nv_bfloat16 *>(L->d13);
-            pg.w2 = reinterpret_cast<const __nv_bfloat16 *>(L->d2);
-            pg.slots = L->cap;
-            pg.u_off = L->d_u_off + p0 + g;
-            pg.u_pairs = L->d_u_pairs + p0;
-            pg.u_slot = L->d_u_slot + p0;
-            pg.nu = nu[g];
-            pg.npairs = (t1 - t0) * K;
-            pg.t0 = t0;
-            pg.t1 = t1;
-            pg.K = K;
-            pg.H = L->H;
-            pg.I = L->I;
-            pg.topk_w = w;
-            pg.x_perm = L->d_xperm;
-            pg.act_perm = L->d_actperm;
-            pg.perm_rows = L->wsT * L->wsK;
-            pg.y = L->d_y;
-            pg.out = reinterpret_cast<__nv_bfloat16 *>(out);
-            pg.status = L->d_status;
-            pg.wait_ns = L->wait_ns;
-            rc = launch_prefill_group(pg, stream);
+        if (compute && t1 > t0 && nu[g] > 0 && path != Path::kDecode) {
+            // tensor-core kernels (gather, gate-up + SiLU-mul, down, combine)
+            rc = launch_tc_group(L, path, tc_group(L, x, w, out, g, t0, t1, K, nu[g], nullptr), stream);
             if (rc) return rc;
-            L->launches += kPrefillKernelsPerGroup;
         } else if (compute && t1 > t0 && nu[g] > 0) {
             const int64_t p0 = (int64_t)t0 * K;
             GroupCompute gc{};
@@ -613,6 +645,34 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
         WISP_CUDA_TRY(cudaEventRecord(L->ev_group[g], stream));
     }
     WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
+    WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
+    return WISP_OK;
+}
+
+// Resident layers run the tensor-core paths without a host round trip: the
+// pager (one group, slots fixed) leaves the group's expert lists and count on
+// the device, the compute kernels read them there and skip the call if the
+// pager rejected it (the gather kernel then records the pager's status in
+// the sticky word, reported by the next call or synchronize).
+int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w, const void *ids, int ids64,
+                        int T, int K, void *out, cudaStream_t stream) {
+    if (T > L->wsT || K > L->wsK) {
+        int rc = drain(L);
+        if (rc) return rc;
+        rc = ensure_ws(L, T, K);
+        if (rc) return rc;
+    }
+    PagerParams p;
+    fill_pager_params(L, p, ids, ids64, T, K, 0, 1);
+    // the layer's workspace: after its previous forward, whichever stream that used
+    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));
+    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
+    int rc = launch_pager(p, stream);
+    if (rc) return rc;
+    ++L->launches;
+    const int nu_bound = (int)std::min<long>(L->E, (long)T * K);
+    rc = launch_tc_group(L, path, tc_group(L, x, w, out, 0, 0, T, K, nu_bound, L->d_dev_hdr + kHdrStatus), stream);
+    if (rc) return rc;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
     return WISP_OK;
 }
@@ -672,6 +732,7 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
         L->mb_busy[slot].store(1);
     }
     fp.pg.mb = L->d_mb + (long)slot * L->mb_words;
+    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));  // the workspace, whichever stream used it last
     WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
     int rc = launch_forward(fp, T, stream);
     if (rc) {
@@ -825,7 +886,10 @@ int wisp_moe_forward(wisp_layer *L, const void *x, const float *topk_weights,
     int rc = take_errors(L);
     if (rc) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (L->async && top_k <= L->cap && !use_prefill_gemm(L, num_tokens, top_k))
+    const Path path = compute_path(L, num_tokens, top_k);
+    if (L->async && num_tokens > 0 && path != Path::kDecode && L->mode == WISP_MODE_RESIDENT)
+        return forward_tc_resident(L, path, x, topk_weights, topk_ids, ids_int64, num_tokens, top_k, out, s);
+    if (L->async && top_k <= L->cap && path == Path::kDecode)
         return forward_async(L, x, topk_weights, topk_ids, ids_int64, num_tokens, top_k, out, s);
     rc = run_pager(L, topk_ids, ids_int64, num_tokens, top_k, 0, 1, s);
     if (rc) return rc;
@@ -1037,6 +1101,10 @@ int wisp_layer_config(wisp_layer *L, int32_t key, int64_t value) {
             return WISP_OK;
         case WISP_CFG_TRACE_BUFFER:
             L->trace = reinterpret_cast<unsigned long long *>(value);
+            return WISP_OK;
+        case WISP_CFG_TC_MIN_PAIRS:
+            if (value < 1) return fail(WISP_ERR_INVALID, "wisp_layer_config: tensor-core threshold below 1 pair");
+            L->tc_min_pairs = (int)std::min<int64_t>(value, kPrefillMinPairs);
             return WISP_OK;
         default:
             return fail(WISP_ERR_INVALID, "wisp_layer_config: unknown key");

@@ -15,7 +15,9 @@ struct PrefillGroup {
     const int32_t *u_off;           // [nu + 1] group-local offsets into u_pairs
     const int32_t *u_pairs;         // [npairs] absolute pair index t * K + k, expert-major
     const int32_t *u_slot;          // [nu]
-    int nu, npairs;
+    const int32_t *nu_dev;          // experts in the group (device word written by the pager)
+    const int32_t *pager_status;    // pager status (device); nullptr when the host checked it
+    int nu, npairs;                 // nu: upper bound of *nu_dev (grid sizes)
     int t0, t1, K, H, I;
     const float *topk_w;            // [T * K]
     __nv_bfloat16 *x_perm;          // [perm_rows][H] workspace
@@ -25,6 +27,7 @@ struct PrefillGroup {
     __nv_bfloat16 *out;             // [T][H]
     int *status;                    // sticky status word
     long long wait_ns;
+    uint32_t *ready;                // weight-stationary path: batch_ready_words(npairs, nu) words
 };
 
 // The tensor-core path covers hidden % 256 == 0 and inter % 128 == 0.
@@ -33,5 +36,14 @@ bool prefill_shapes_supported(int H, int I);
 // Launches gather, gate-up GEMM, down GEMM and combine (4 kernels) on `stream`.
 constexpr int kPrefillKernelsPerGroup = 4;
 int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream);
+
+// Weight-stationary tensor-core path for decode batches (few tokens per
+// expert): gather, one persistent gate-up + down launch, combine (3 kernels).
+constexpr int kBatchKernelsPerGroup = 3;
+constexpr int kBatchTokens = 32;  // token rows per tile (the MMA's N)
+// Per-token-block counters (+ one abort word) the path needs for a group of
+// `npairs` pairs over at most `nu` experts.
+inline long batch_ready_words(long npairs, long nu) { return nu + (npairs + kBatchTokens - 1) / kBatchTokens + 1; }
+int launch_batch_group(const PrefillGroup &p, cudaStream_t stream);
 
 }  // namespace wisp

@@ -300,17 +300,18 @@ class WispMoEState:
                 "unique_experts": info[3], "kernel_launches": n.value}
 
     def configure(self, *, asynchronous: bool | None = None, wait_ns: int | None = None,
-                  drop_pageins: int | None = None) -> None:
+                  drop_pageins: int | None = None, tc_min_pairs: int | None = None) -> None:
         """Runtime knobs of the native layer (see ``wisp_layer_config``).
 
         ``asynchronous``: the single-launch forward (default for resident
         layers).  A paged layer defaults to the host-synchronous forward: a
         paged single-launch forward waits inside its kernel for page-in copies
         a host thread issues after the launch, so it suits only callers that
-        queue no other device work while it pages in."""
+        queue no other device work while it pages in.  ``tc_min_pairs``: calls
+        of at least this many (token, k) pairs compute on the tensor cores."""
         L = _lib.lib()
         for key, val in ((_lib.CFG_ASYNC, asynchronous), (_lib.CFG_WAIT_NS, wait_ns),
-                         (_lib.CFG_DROP_PAGEINS, drop_pageins)):
+                         (_lib.CFG_DROP_PAGEINS, drop_pageins), (_lib.CFG_TC_MIN_PAIRS, tc_min_pairs)):
             if val is not None:
                 _lib.check(L.wisp_layer_config(self._h, key, int(val)), "configure")
 
