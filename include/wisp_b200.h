@@ -159,14 +159,21 @@ WISP_API int wisp_layer_sync(wisp_layer *layer);
  * weight-stationary tiles up to 256 pairs, token-major GEMMs above -- where
  * hidden % 256 == 0 and inter % 128 == 0; smaller calls on the CUDA-core
  * decode kernels.  The choice depends on the call size only, so outputs stay
- * byte-identical across caps and modes; default 64, capped at 257).
+ * byte-identical across caps and modes; default 64, capped at 257),
+ * WISP_CFG_COMPUTE_CLASS (0: by call size as above, the default; 1: the
+ * CUDA-core kernels at any size; 2: the tensor cores at any size.  The two
+ * tensor-core paths give identical bytes, the CUDA-core kernels differ in
+ * the fp32 accumulation order: an expert-parallel owner computes each
+ * source's rows in the class a one-GPU call of that source's size would
+ * use).
  */
 enum wisp_config_key {
     WISP_CFG_ASYNC = 1,
     WISP_CFG_WAIT_NS = 2,
     WISP_CFG_DROP_PAGEINS = 4,
     WISP_CFG_TRACE_BUFFER = 5,
-    WISP_CFG_TC_MIN_PAIRS = 6
+    WISP_CFG_TC_MIN_PAIRS = 6,
+    WISP_CFG_COMPUTE_CLASS = 7
 };
 WISP_API int wisp_layer_config(wisp_layer *layer, int32_t key, int64_t value);
 

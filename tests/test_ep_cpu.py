@@ -24,8 +24,14 @@ class _FakeExperts:
     """y = x * (global id + 1) * w, stored bf16; records the ids it saw."""
 
     def __init__(self, rank, per):
-        self.rank, self.per, self.seen = rank, per, []
+        self.rank, self.per, self.seen, self.classes = rank, per, [], []
         self.hidden_size, self.device = H, torch.device("cpu")
+
+    def compute_class(self, pairs):
+        return "tc" if pairs >= 10 else "cuda"
+
+    def configure(self, compute_class=None):
+        self.classes.append(compute_class)
 
     def forward(self, x, w, ids, out):
         self.seen.append(ids.reshape(-1).clone())
@@ -94,6 +100,10 @@ def _worker(rank, world, port):
                 expect.append(mine - rank * per)
             seen = local.seen[-1] if len(torch.cat(expect)) else torch.empty(0, dtype=torch.int32)
             assert torch.equal(seen.long(), torch.cat(expect)), f"rank {rank}: receive order"
+            if len(torch.cat(expect)):
+                # every source called with T * K = 15 pairs: one call, forced to that
+                # class, then back to the size rule
+                assert local.classes[-2:] == ["tc", "auto"], local.classes
         # an id out of range on rank 1 only: every rank raises, nothing left pending
         x, w, ids = _routing(rank, 9)
         if rank == 1:

@@ -5,7 +5,9 @@
   the send buffers the way the collective would.  The output must be
   byte-identical to the one-GPU layer over all experts, and each paged rank's
   pager state must equal the oracle pager over its shard fed the rows it
-  received, in (source rank, pair) order.
+  received, in (source rank, pair) order.  Call sizes on either side of the
+  tensor-core threshold (64 pairs), also mixed across ranks: each owner
+  computes a source's rows in the class of that source's call size.
 * Two real ranks over NCCL (needs two GPUs; skipped otherwise): the same
   byte identity through torch.distributed.
 """
@@ -49,7 +51,8 @@ def emulated_forward(layers, xs, ws, idss):
     for r in range(P):
         recv_x.append(torch.cat([plans[s].send_x[offs[s][r]:offs[s][r + 1]] for s in range(P)]))
         recv_m.append(torch.cat([plans[s].send_meta[offs[s][r]:offs[s][r + 1]] for s in range(P)]))
-    recv_y = [layers[r].compute(recv_x[r], recv_m[r]) for r in range(P)]
+    src_pairs = [plans[s].num_tokens * plans[s].top_k for s in range(P)]
+    recv_y = [layers[r].compute(recv_x[r], recv_m[r], plans[r].recv_counts, src_pairs) for r in range(P)]
     outs = []
     for s in range(P):
         parts = []
@@ -60,11 +63,16 @@ def emulated_forward(layers, xs, ws, idss):
     return outs, recv_x, recv_m, recv_y
 
 
-@pytest.mark.parametrize("P,cap,mode", [(2, 8, "resident"), (2, 3, "paged"), (4, 2, "paged"),
-                                        (4, 4, "resident")])
-def test_ep_emulated_ranks_match_one_gpu(P, cap, mode):
+@pytest.mark.parametrize("P,cap,mode,K,Ts", [
+    (2, 8, "resident", 4, (6, 6)), (2, 3, "paged", 4, (6, 6)), (4, 2, "paged", 4, (6, 6, 6, 6)),
+    (4, 4, "resident", 4, (6, 6, 6, 6)),
+    (4, 4, "resident", 8, (8, 8, 8, 8)),      # 64 pairs per source: tensor cores, owners get ~64 rows
+    (2, 8, "resident", 8, (12, 3)),           # one source above the threshold, one below
+    (2, 8, "paged", 8, (12, 12)),
+])
+def test_ep_emulated_ranks_match_one_gpu(P, cap, mode, K, Ts):
     from wisp_b200.integrations.vllm.fused_moe import WispMoEState
-    E, H, I, K, T = 16, 512, 256, 4, 6
+    E, H, I = 16, 512, 256
     w13, w2, g = _weights(E, H, I, 3)
     layers = []
     oracles = []
@@ -77,6 +85,7 @@ def test_ep_emulated_ranks_match_one_gpu(P, cap, mode):
     for step in range(4):
         xs, ws, idss = [], [], []
         for r in range(P):
+            T = Ts[r]
             w, ids = wl.softmax_topk(torch.randn(T, E, generator=g), K)
             xs.append(torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV))
             ws.append(w.to(DEV))

@@ -28,6 +28,9 @@ CFG_WAIT_NS = 2
 CFG_DROP_PAGEINS = 4
 CFG_TRACE_BUFFER = 5
 CFG_TC_MIN_PAIRS = 6
+CFG_COMPUTE_CLASS = 7
+TC_MIN_PAIRS_DEFAULT = 64   # the library's default tensor-core threshold (pairs)
+PREFILL_MIN_PAIRS = 257     # calls from this size always run on the tensor cores
 
 _c_int32 = ctypes.c_int32
 _c_int64 = ctypes.c_int64

@@ -17,20 +17,29 @@
 //            Y0 / Y1 [128 x 32] = W2 rows h / h + 128 . act_perm rows^T over
 //            K = I; y[pair][h + r] = bf16(acc * routing weight).
 //
-// A token block is up to 32 consecutive rows of one expert in the group's
-// expert-major pair order (X_perm, written by the gather kernel), so each
-// weight tile is streamed once per token block, i.e. once per expert for a
-// decode batch.  Gate-up and down share ONE persistent launch: tiles are
-// numbered gate-up first, then down, both in token-block order, and each CTA
-// walks its tiles (t = blockIdx.x, + gridDim.x, ...) in that order.  Before
-// the producer loads a down tile it waits until the block's gate-up tiles
-// have published their activation rows: every epilogue warp adds 1 to the
-// block's counter after its stores (release at GPU scope, after an
-// async-proxy fence, since the rows are read back by TMA), and the producer
-// waits for 4 * I / 128 (acquire, then an async-proxy fence).  Gate-up tiles
-// wait for nothing, and the launch is cooperative (every CTA resident), so
-// these waits end; each is bounded all the same and a CTA that gives up
-// raises a device-wide abort word that ends the others' waits.
+// A token block is up to 32 consecutive rows of one expert in the call's
+// expert-major pair order, so each weight tile is streamed once per token
+// block, i.e. once per expert for a decode batch.  Gate-up and down share ONE
+// persistent launch: tiles are numbered gate-up first, then down, both in
+// token-block order, and each CTA walks its tiles (t = blockIdx.x,
+// + gridDim.x, ...) in that order.  Before the producer loads a down tile it
+// waits until the block's gate-up tiles have published their activation rows:
+// every epilogue warp adds 1 to the block's counter after its stores (release
+// at GPU scope, after an async-proxy fence, since the rows are read back by
+// TMA), and the producer waits for 4 * I / 128 (acquire, then an async-proxy
+// fence).  Gate-up tiles wait for nothing, and the launch is cooperative
+// (every CTA resident), so these waits end; each is bounded all the same and
+// a CTA that gives up raises a device-wide abort word that ends the others'
+// waits.  The counters come in two halves by launch parity: a launch uses one
+// and zeroes the other for the next launch.
+//
+// The expert lists come either from the pager (paged layers: u_off / u_pairs
+// / u_slot in global memory, X_perm written by the gather kernel) or, for a
+// resident layer's call, from the kernel itself: every CTA sorts the call's
+// (at most 256) pairs by expert in shared memory -- experts ascending, pairs
+// ascending within an expert, slots from the expert map -- and copies the
+// hidden rows of the token blocks of its own gate-up tiles into X_perm before
+// its producer starts (CTAs that share a block write identical bytes).
 //
 // Roles per CTA (192 threads, one CTA per SM): warp 0 lane 0 issues the TMA
 // loads of a 6-stage ring (two 128 x 64 weight boxes and one 32 x 64 token
@@ -42,7 +51,7 @@
 //
 // Each output element is its own dot product with the K blocks in order, so
 // results do not depend on which tokens or experts share a tile, the slots,
-// the cap or the grouping.
+// the cap or the grouping; they are byte-identical to the token-major GEMMs'.
 #include "gemm_sm100.cuh"
 #include "prefill.cuh"
 
@@ -82,22 +91,35 @@ constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + slack to align st
 constexpr int kAccCols = 2 * kTN;                 // one tile: two accumulators of kTN columns
 constexpr int kTmemCols = 2 * kAccCols;           // double-buffered
 constexpr int kDownRows = 2 * kWM;                // hidden rows per down tile
-constexpr int kMaxExperts = 1024;
+constexpr int kMaxPairs = kBatchMaxPairs;
+constexpr int kMaxRouteExperts = 1024;
 static_assert(kTmemCols >= 32 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation: power of two >= 32");
-static_assert(kTN % 16 == 0 && kTN >= 16 && kTN <= 256, "MMA N for M = 128");
+static_assert(kTN == 32, "the epilogue reads one 32-column TMEM block per accumulator");
+static_assert(3 * kMaxRouteExperts * 4 + kMaxPairs * 4 <= kStages * kStageBytes, "routing scratch fits the ring");
 
 struct Args {
-    const int32_t *u_off;     // [nu + 1]
-    const int32_t *u_pairs;   // [npairs] absolute pair index, expert-major
-    const int32_t *u_slot;    // [nu]
+    // lists from the pager (route == false)
+    const int32_t *u_off;       // [nu + 1]
+    const int32_t *u_pairs;     // [npairs] absolute pair index, expert-major
+    const int32_t *u_slot;      // [nu]
     const int32_t *nu_dev;
     const int32_t *pager_status;
+    // in-kernel routing (route == true)
+    int route;
+    const void *ids;
+    int ids64, T, K, E, count_forward;
+    const int32_t *emap;
+    const uint4 *x;             // [T][H / 8]
+    uint4 *x_perm;              // [npairs][H / 8]
+    int64_t *hdr;
+    int32_t *dev_status;
+    // both
     int H, I;
-    const float *topk_w;      // [T * K]
-    __nv_bfloat16 *act_perm;  // [npairs][I]
-    __nv_bfloat16 *y;         // [T * K][H]
-    uint32_t *ready;          // [blocks] gate-up warps done per token block; [nready - 1] abort word
-    int nready;
+    const float *topk_w;        // [T * K]
+    __nv_bfloat16 *act_perm;    // [npairs][I]
+    __nv_bfloat16 *y;           // [T * K][H]
+    uint32_t *ready;            // this launch's counters; [kBatchReadyWords - 1] abort word
+    uint32_t *ready_next;       // the other half, zeroed for the next launch
     int *status;
     long long wait_ns;
 };
@@ -110,25 +132,28 @@ struct Ring {
     int issued, consumed;
 };
 
-struct BlockTable {
-    int nu, nblocks;
-    int off[kMaxExperts + 1];    // pair-list offsets
-    int first[kMaxExperts + 1];  // first token block of each expert (prefix of block counts)
+// The call's (or group's) experts, their token blocks and pair lists.
+struct Lists {
+    int nu, nblocks, bad;
+    int off[kMaxPairs + 1];    // pair-list offsets
+    int first[kMaxPairs + 1];  // first token block of each expert (prefix of block counts)
+    int pairs[kMaxPairs];      // routed lists: absolute pair index, expert-major
+    int slot[kMaxPairs];       // routed lists: slot of each expert
 };
 
 // Token block b -> expert u, first list position q0, rows.
-__device__ __forceinline__ void block_of(const BlockTable &bt, int b, int &u, int &q0, int &rows) {
-    int lo = 0, hi = bt.nu - 1;
+__device__ __forceinline__ void block_of(const Lists &L, int b, int &u, int &q0, int &rows) {
+    int lo = 0, hi = L.nu - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (bt.first[mid] <= b)
+        if (L.first[mid] <= b)
             lo = mid;
         else
             hi = mid - 1;
     }
     u = lo;
-    q0 = bt.off[u] + (b - bt.first[u]) * kTN;
-    rows = min(kTN, bt.off[u + 1] - q0);
+    q0 = L.off[u] + (b - L.first[u]) * kTN;
+    rows = min(kTN, L.off[u + 1] - q0);
 }
 
 struct Tile {
@@ -162,13 +187,13 @@ __device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
 __device__ __forceinline__ void give_up(Ring &R, const Args &g) {
     R.abort = 1;
     if (g.status) *reinterpret_cast<volatile int *>(g.status) = WISP_ERR_TIMEOUT;
-    atomicExch(g.ready + g.nready - 1, 1u);  // ends the other CTAs' waits
+    atomicExch(g.ready + kBatchReadyWords - 1, 1u);  // ends the other CTAs' waits
 }
 
 // Producer wait for a down tile: the block's activation rows are published.
 __device__ __forceinline__ bool wait_ready(const Args &g, int b, uint32_t need, volatile int *abort) {
     const uint32_t *word = g.ready + b;
-    const volatile uint32_t *abort_all = g.ready + g.nready - 1;
+    const volatile uint32_t *abort_all = g.ready + kBatchReadyWords - 1;
     if (ld_acquire_gpu(word) < need) {
         const unsigned long long t0 = globaltimer_ns();
         while (ld_acquire_gpu(word) < need) {
@@ -186,31 +211,158 @@ __device__ __forceinline__ unsigned char *align1024(unsigned char *p) {
     return p + ((1024u - (a & 1023u)) & 1023u);
 }
 
+// Every CTA: the call's pairs sorted by expert (experts ascending, pairs
+// ascending within one), with the ring as scratch.  Sets L.bad on an id
+// outside [0, E).
+__device__ void route_pairs(const Args &g, Lists &L, unsigned char *scratch) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int E = g.E, P = g.T * g.K;
+    int *cnt = reinterpret_cast<int *>(scratch);  // [E] pairs per expert
+    int *base = cnt + kMaxRouteExperts;           // [E] next list position of each expert
+    int *ids = base + kMaxRouteExperts;           // [P]
+    for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    bool bad = false;
+    for (int p = tid; p < P; p += blockDim.x) {
+        const long long v = g.ids64 ? reinterpret_cast<const int64_t *>(g.ids)[p]
+                                    : (long long)reinterpret_cast<const int32_t *>(g.ids)[p];
+        const bool ok = v >= 0 && v < E;
+        bad |= !ok;
+        ids[p] = ok ? (int)v : 0;
+        if (ok) atomicAdd(&cnt[(int)v], 1);
+    }
+    if (__syncthreads_or(bad)) {
+        if (tid == 0) L.bad = 1;
+        __syncthreads();
+        return;
+    }
+    if (warp == 0) {
+        // experts in contiguous chunks per lane: scan of pair and expert counts
+        const int chunk = (E + 31) / 32, e0 = min(E, lane * chunk), e1 = min(E, e0 + chunk);
+        int np = 0, nu = 0;
+        for (int e = e0; e < e1; ++e) {
+            np += cnt[e];
+            nu += cnt[e] > 0;
+        }
+        int ip = np, iu = nu;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a = __shfl_up_sync(0xffffffffu, ip, o), b = __shfl_up_sync(0xffffffffu, iu, o);
+            if (lane >= o) {
+                ip += a;
+                iu += b;
+            }
+        }
+        int at = ip - np, u = iu - nu;
+        for (int e = e0; e < e1; ++e) {
+            const int c = cnt[e];
+            if (c > 0) {
+                L.off[u] = at;
+                L.slot[u] = g.emap[e];
+                base[e] = at;
+                ++u;
+                at += c;
+            }
+        }
+        if (lane == 31) {
+            L.nu = iu;
+            L.off[iu] = P;
+        }
+        __syncwarp();
+        // placement, 32 pairs at a time in ascending order
+        for (int c0 = 0; c0 < P; c0 += 32) {
+            const int p = c0 + lane;
+            const int e = p < P ? ids[p] : -1 - lane;
+            const unsigned peers = __match_any_sync(0xffffffffu, e);
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            if (p < P) L.pairs[base[e] + rank] = p;
+            __syncwarp();
+            if (p < P && rank == 0) base[e] += __popc(peers);
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     batch_moe_kernel(const __grid_constant__ CUtensorMap map_w13, const __grid_constant__ CUtensorMap map_w2,
                      const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_act,
                      const Args g) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ Ring R;
-    __shared__ BlockTable bt;
+    __shared__ Lists L;
     unsigned char *stages = align1024(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = g.H, I = g.I;
 
-    // ---- setup: block table, barriers, TMEM ----------------------------------------
-    const int nu = min(gemm::group_experts(g.nu_dev, g.pager_status), kMaxExperts);
-    for (int i = threadIdx.x; i <= nu; i += blockDim.x) bt.off[i] = g.u_off[i];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        bt.nu = nu;
-        int acc = 0;
-        for (int e = 0; e < nu; ++e) {
-            bt.first[e] = acc;
-            acc += (bt.off[e + 1] - bt.off[e] + kTN - 1) / kTN;
+    // the next launch's counters
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kBatchReadyWords; i += gridDim.x * blockDim.x)
+        g.ready_next[i] = 0;
+    // the combine may be scheduled now (it waits for this grid's completion)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    // ---- the expert lists ----------------------------------------------------------
+    const int32_t *pairs;
+    if (g.route) {
+        if (threadIdx.x == 0) L.bad = 0;
+        __syncthreads();
+        route_pairs(g, L, stages);
+        if (L.bad) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) {
+                *reinterpret_cast<volatile int32_t *>(g.dev_status) = WISP_ERR_BAD_EXPERT;
+                if (g.status) *reinterpret_cast<volatile int *>(g.status) = WISP_ERR_BAD_EXPERT;
+            }
+            return;
         }
-        bt.first[nu] = acc;
-        bt.nblocks = acc;
+        pairs = L.pairs;
+    } else {
+        const int nu = min(gemm::group_experts(g.nu_dev, g.pager_status), kMaxPairs);
+        for (int i = threadIdx.x; i <= nu; i += blockDim.x) L.off[i] = g.u_off[i];
+        for (int i = threadIdx.x; i < nu; i += blockDim.x) L.slot[i] = g.u_slot[i];
+        if (threadIdx.x == 0) L.nu = nu;
+        pairs = g.u_pairs;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int e = 0; e < L.nu; ++e) {
+            L.first[e] = acc;
+            acc += (L.off[e + 1] - L.off[e] + kTN - 1) / kTN;
+        }
+        L.first[L.nu] = acc;
+        L.nblocks = acc;
         R.abort = 0;
         R.issued = R.consumed = 0;
+        if (g.route && blockIdx.x == 0) {
+            // the pager's resident-mode bookkeeping: the forward, one group, its experts
+            if (g.count_forward) g.hdr[1] += 1;
+            g.hdr[5] += 1;
+            g.hdr[6] += L.nu;
+            *reinterpret_cast<volatile int32_t *>(g.dev_status) = WISP_OK;
+        }
+    }
+    __syncthreads();
+    const int cj = I / kWM, ch = H / kDownRows;
+    const int ngu = L.nblocks * cj;
+    const int ntiles = ngu + L.nblocks * ch;
+    if ((int)blockIdx.x >= ntiles) return;
+
+    if (g.route) {
+        // hidden rows of this CTA's gate-up blocks into X_perm (read back by TMA)
+        const int H8 = H / 8;
+        for (int t = blockIdx.x; t < ngu; t += gridDim.x) {
+            int u, q0, rows;
+            block_of(L, t / cj, u, q0, rows);
+            for (int i = threadIdx.x; i < rows * H8; i += blockDim.x) {
+                const int q = q0 + i / H8, c = i % H8;
+                g.x_perm[(size_t)q * H8 + c] = g.x[(size_t)(L.pairs[q] / g.K) * H8 + c];
+            }
+        }
+        fence_proxy_async_global();
+    }
+    __syncthreads();  // the ring is no longer scratch
+
+    if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&R.full[s], 1);
             mbar_init(&R.empty[s], 1);
@@ -223,12 +375,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    __syncthreads();
-    const int H = g.H, I = g.I;
-    const int cj = I / kWM, ch = H / kDownRows;
-    const int ngu = bt.nblocks * cj;
-    const int ntiles = ngu + bt.nblocks * ch;
-    if ((int)blockIdx.x >= ntiles) return;
     if (warp == 0) tmem_alloc(&R.tmem_base, kTmemCols);
     tc_fence_before();
     __syncthreads();
@@ -244,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
                 const Tile tl = tile_at(t, ngu, cj, ch);
                 int u, q0, rows;
-                block_of(bt, tl.b, u, q0, rows);
-                const int slot = g.u_slot[u];
+                block_of(L, tl.b, u, q0, rows);
+                const int slot = L.slot[u];
                 const CUtensorMap *mw, *mt;
                 int a0, a1, kbc;
                 if (!tl.down) {
@@ -338,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const Tile tl = tile_at(t, ngu, cj, ch);
             int u, q0, rows;
-            block_of(bt, tl.b, u, q0, rows);
+            block_of(L, tl.b, u, q0, rows);
             const uint32_t tbase = R.tmem_base + (i & 1) * kAccCols + ((uint32_t)(quarter * 32) << 16);
             uint32_t d0[kTN], d1[kTN];
             tmem_ld32(tbase, d0);
@@ -366,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int n = 0; n < kTN; ++n) {
                     if (n < rows) {
-                        const int p = g.u_pairs[q0 + n];
+                        const int p = pairs[q0 + n];
                         const float wp = g.topk_w[p];
                         __nv_bfloat16 *dst = g.y + (size_t)p * H + h;
                         dst[0] = __float2bfloat16_rn(__uint_as_float(d0[n]) * wp);
@@ -392,15 +538,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) tmem_dealloc(R.tmem_base, kTmemCols);
 }
 
-}  // namespace
-}  // namespace batch
-
-int launch_batch_group(const PrefillGroup &p, cudaStream_t stream) {
-    using namespace batch;
-    if (!prefill_shapes_supported(p.H, p.I))
-        return set_error("wisp: tensor-core path needs hidden % 256 == 0 and inter % 128 == 0"), WISP_ERR_UNSUPPORTED;
-    if (p.npairs <= 0 || p.nu <= 0) return WISP_OK;
-    if (!p.ready) return set_error("wisp: batch path without its counter workspace"), WISP_ERR_INVALID;
+// Shared launch of the persistent kernel (cooperative: at most one CTA per
+// SM, all resident -- the down tiles wait for gate-up tiles of other CTAs).
+int launch_kernel(const PrefillGroup &p, const Args &a, long nu_bound, cudaStream_t stream) {
     static bool attr_set[64] = {};
     int dev = 0;
     WISP_CUDA_TRY(cudaGetDevice(&dev));
@@ -415,31 +555,12 @@ int launch_batch_group(const PrefillGroup &p, cudaStream_t stream) {
     if (!rc) rc = gemm::make_map(&mx, p.x_perm, (uint64_t)p.perm_rows, (uint64_t)p.H, kTN);
     if (!rc) rc = gemm::make_map(&mact, p.act_perm, (uint64_t)p.perm_rows, (uint64_t)p.I, kTN);
     if (rc) return rc;
-    Args a{};
-    a.u_off = p.u_off;
-    a.u_pairs = p.u_pairs;
-    a.u_slot = p.u_slot;
-    a.nu_dev = p.nu_dev;
-    a.pager_status = p.pager_status;
-    a.H = p.H;
-    a.I = p.I;
-    a.topk_w = p.topk_w;
-    a.act_perm = p.act_perm;
-    a.y = p.y;
-    a.ready = p.ready;
-    a.nready = (int)batch_ready_words(p.npairs, p.nu);
-    a.status = p.status;
-    a.wait_ns = p.wait_ns;
-    rc = gemm::launch_gather(p, a.ready, a.nready, stream);
-    if (rc) return rc;
-    // persistent and cooperative: at most one CTA per SM, all resident (the
-    // down tiles wait for gate-up tiles of other CTAs)
     int sms = 0;
     WISP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const long blocks = std::min<long>(p.nu, p.npairs) + (p.npairs + kTN - 1) / kTN;
+    const long blocks = std::min<long>(nu_bound, p.npairs) + (p.npairs + kTN - 1) / kTN;
     const long tiles = blocks * (p.I / kWM + p.H / kDownRows);
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)std::min<long>(tiles, sms));
+    cfg.gridDim = dim3((unsigned)std::max<long>(1, std::min<long>(tiles, sms)));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = stream;
@@ -449,7 +570,75 @@ int launch_batch_group(const PrefillGroup &p, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     WISP_CUDA_TRY(cudaLaunchKernelEx(&cfg, batch_moe_kernel, mw13, mw2, mx, mact, a));
-    return gemm::launch_combine(p, stream);
+    return WISP_OK;
+}
+
+int check_group(const PrefillGroup &p, const uint32_t *ready_next) {
+    if (!prefill_shapes_supported(p.H, p.I))
+        return set_error("wisp: tensor-core path needs hidden % 256 == 0 and inter % 128 == 0"), WISP_ERR_UNSUPPORTED;
+    if (p.npairs > kMaxPairs)
+        return set_error("wisp: weight-stationary path takes at most 256 pairs per call"), WISP_ERR_INVALID;
+    if (!p.ready || !ready_next) return set_error("wisp: batch path without its counters"), WISP_ERR_INVALID;
+    return WISP_OK;
+}
+
+Args common_args(const PrefillGroup &p, uint32_t *ready_next) {
+    Args a{};
+    a.H = p.H;
+    a.I = p.I;
+    a.topk_w = p.topk_w;
+    a.act_perm = p.act_perm;
+    a.y = p.y;
+    a.ready = p.ready;
+    a.ready_next = ready_next;
+    a.status = p.status;
+    a.wait_ns = p.wait_ns;
+    return a;
+}
+
+}  // namespace
+}  // namespace batch
+
+int launch_batch_group(const PrefillGroup &p, uint32_t *ready_next, cudaStream_t stream) {
+    using namespace batch;
+    int rc = check_group(p, ready_next);
+    if (rc || p.npairs <= 0 || p.nu <= 0) return rc;
+    Args a = common_args(p, ready_next);
+    a.u_off = p.u_off;
+    a.u_pairs = p.u_pairs;
+    a.u_slot = p.u_slot;
+    a.nu_dev = p.nu_dev;
+    a.pager_status = p.pager_status;
+    rc = gemm::launch_gather(p, stream);
+    if (!rc) rc = launch_kernel(p, a, p.nu, stream);
+    if (!rc) rc = gemm::launch_combine(p, stream, true);
+    return rc;
+}
+
+int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, uint32_t *ready_next, cudaStream_t stream) {
+    using namespace batch;
+    int rc = check_group(p, ready_next);
+    if (rc || p.npairs <= 0) return rc;
+    if (r.E < 1 || r.E > kMaxRouteExperts)
+        return set_error("wisp: in-kernel routing takes at most 1024 experts"), WISP_ERR_INVALID;
+    Args a = common_args(p, ready_next);
+    a.route = 1;
+    a.ids = r.ids;
+    a.ids64 = r.ids64;
+    a.T = p.t1 - p.t0;
+    a.K = p.K;
+    a.E = r.E;
+    a.count_forward = r.count_forward;
+    a.emap = r.emap;
+    a.x = reinterpret_cast<const uint4 *>(p.x);
+    a.x_perm = reinterpret_cast<uint4 *>(p.x_perm);
+    a.hdr = r.hdr;
+    a.dev_status = r.dev_status;
+    PrefillGroup pc = p;
+    pc.pager_status = r.dev_status;  // the combine leaves out alone after a rejected call
+    rc = launch_kernel(p, a, std::min(r.E, p.npairs), stream);
+    if (!rc) rc = gemm::launch_combine(pc, stream, true);
+    return rc;
 }
 
 }  // namespace wisp

@@ -15,12 +15,12 @@ __device__ __forceinline__ unsigned char *align1024(unsigned char *p) {
     return p + ((1024u - (a & 1023u)) & 1023u);
 }
 
-// X_perm[q] = x[token of pair q]: one warp per row, 16-byte copies.  Also
-// zeroes the weight-stationary path's per-block counters (`ready`).  When the
-// pager ran without a host check and rejected the call, the lists are stale:
-// nothing is read and block 0 records the pager's status in the sticky word.
+// X_perm[q] = x[token of pair q]: one warp per row, 16-byte copies.  When
+// the pager ran without a host check and rejected the call, the lists are
+// stale: nothing is read and block 0 records the pager's status in the
+// sticky word.
 __global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int K, int H8, uint4 *xp,
-                              uint32_t *ready, int nready, const int32_t *pager_status, int *status) {
+                              const int32_t *pager_status, int *status) {
     if (pager_status) {
         const int st = *reinterpret_cast<const volatile int32_t *>(pager_status);
         if (st != WISP_OK) {
@@ -28,8 +28,6 @@ __global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int
             return;
         }
     }
-    if (ready)
-        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nready; i += gridDim.x * blockDim.x) ready[i] = 0;
     const int q = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (q >= P) return;
     const uint4 *src = x + (size_t)(u_pairs[q] / K) * H8;
@@ -247,8 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // out[t] = sum over k in routing order of y[t * K + k], t in [t0, t1).
+// May run as a programmatic dependent launch: waits for the producing grid.
 __global__ void combine_kernel(const uint4 *y, int t0, int t1, int K, int H8, uint4 *out,
                                const int32_t *pager_status) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (pager_status && *reinterpret_cast<const volatile int32_t *>(pager_status) != WISP_OK) return;
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long)(t1 - t0) * H8) return;
@@ -306,24 +306,31 @@ int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, u
     return WISP_OK;
 }
 
-int launch_gather(const PrefillGroup &p, uint32_t *ready, int nready, cudaStream_t stream) {
+int launch_gather(const PrefillGroup &p, cudaStream_t stream) {
     const int warps = 8;
-    const int blocks = std::max((p.npairs + warps - 1) / warps, ready ? (nready + warps * 32 - 1) / (warps * 32) : 0);
+    const int blocks = (p.npairs + warps - 1) / warps;
     if (blocks <= 0) return WISP_OK;
     gather_kernel<<<blocks, warps * 32, 0, stream>>>(reinterpret_cast<const uint4 *>(p.x), p.u_pairs, p.npairs, p.K,
-                                                     p.H / 8, reinterpret_cast<uint4 *>(p.x_perm), ready, nready,
-                                                     p.pager_status, p.status);
+                                                     p.H / 8, reinterpret_cast<uint4 *>(p.x_perm), p.pager_status,
+                                                     p.status);
     WISP_CUDA_TRY(cudaGetLastError());
     return WISP_OK;
 }
 
-int launch_combine(const PrefillGroup &p, cudaStream_t stream) {
+int launch_combine(const PrefillGroup &p, cudaStream_t stream, bool dependent) {
     const long n = (long)(p.t1 - p.t0) * (p.H / 8);
     if (n <= 0) return WISP_OK;
-    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-        reinterpret_cast<const uint4 *>(p.y), p.t0, p.t1, p.K, p.H / 8, reinterpret_cast<uint4 *>(p.out),
-        p.pager_status);
-    WISP_CUDA_TRY(cudaGetLastError());
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((n + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    WISP_CUDA_TRY(cudaLaunchKernelEx(&cfg, combine_kernel, reinterpret_cast<const uint4 *>(p.y), p.t0, p.t1, p.K,
+                                     p.H / 8, reinterpret_cast<uint4 *>(p.out), p.pager_status));
     return WISP_OK;
 }
 
@@ -374,13 +381,13 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
     const long mtiles = (long)p.nu + (p.npairs + kBM - 1) / kBM;
     const int grid_gu = (int)std::min<long>(mtiles * (p.I / kHalfN), sms);
     const int grid_dn = (int)std::min<long>(mtiles * (p.H / kBN), sms);
-    rc = launch_gather(p, nullptr, 0, stream);
+    rc = launch_gather(p, stream);
     if (rc) return rc;
     gateup_gemm_kernel<<<grid_gu, kThreads, kSmemBytes, stream>>>(mx, mw13, g);
     WISP_CUDA_TRY(cudaGetLastError());
     down_gemm_kernel<<<grid_dn, kThreads, kSmemBytes, stream>>>(mact, mw2, g);
     WISP_CUDA_TRY(cudaGetLastError());
-    return launch_combine(p, stream);
+    return launch_combine(p, stream, false);
 }
 
 }  // namespace wisp

@@ -298,10 +298,11 @@ __device__ __forceinline__ int group_experts(const int32_t *nu_dev, const int32_
 // Row-major bf16 matrix [rows][cols] (16-byte aligned base, cols % 8 == 0) as
 // 64 x box_rows boxes with 128-byte swizzle.
 int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_rows);
-// X_perm rows of the group (and, when `ready` is set, zero `nready` words of it).
-int launch_gather(const PrefillGroup &p, uint32_t *ready, int nready, cudaStream_t stream);
-// out rows [t0, t1) = routing-order sum of the weighted rows y.
-int launch_combine(const PrefillGroup &p, cudaStream_t stream);
+// X_perm rows of the group.
+int launch_gather(const PrefillGroup &p, cudaStream_t stream);
+// out rows [t0, t1) = routing-order sum of the weighted rows y; `dependent`:
+// a programmatic dependent launch of the kernel queued before it.
+int launch_combine(const PrefillGroup &p, cudaStream_t stream, bool dependent);
 
 }  // namespace gemm
 }  // namespace wisp

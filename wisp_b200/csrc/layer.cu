@@ -120,8 +120,10 @@ struct wisp_layer {
             *d_counters = nullptr, *d_dev_hdr = nullptr;
     __nv_bfloat16 *d_act = nullptr, *d_y = nullptr;
     __nv_bfloat16 *d_xperm = nullptr, *d_actperm = nullptr;  // tensor-core paths: rows, expert-major
-    uint32_t *d_ready = nullptr;     // weight-stationary path: per-token-block counters
+    uint32_t *d_ready = nullptr;     // weight-stationary path: per-token-block counters, two halves
+    int ready_parity = 0;            // the half the next weight-stationary launch uses
     int tc_min_pairs = kDefaultTcMinPairs;  // calls of at least this many pairs run on the tensor cores
+    int compute_class = 0;           // 0: by call size; 1: CUDA-core kernels; 2: tensor cores
     int32_t *h_mb = nullptr, *d_mb = nullptr;  // kMbRing mailboxes of mb_words words
     long mb_words = 0;
     int mb_next = 0;
@@ -375,7 +377,9 @@ int ensure_ws(wisp_layer *L, int T, int K) {
         if (prefill_shapes_supported(L->H, L->I)) {
             WISP_CUDA_TRY(cudaMalloc(&L->d_xperm, sizeof(__nv_bfloat16) * P * H));
             WISP_CUDA_TRY(cudaMalloc(&L->d_actperm, sizeof(__nv_bfloat16) * P * I));
-            WISP_CUDA_TRY(cudaMalloc(&L->d_ready, sizeof(uint32_t) * batch_ready_words((long)P, (long)P)));
+            WISP_CUDA_TRY(cudaMalloc(&L->d_ready, sizeof(uint32_t) * 2 * kBatchReadyWords));
+            WISP_CUDA_TRY(cudaMemset(L->d_ready, 0, sizeof(uint32_t) * 2 * kBatchReadyWords));
+            L->ready_parity = 0;
         }
     }
     const long words = (mailbox_words(nT, nK) + 31) & ~31L;
@@ -534,8 +538,9 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
 enum class Path { kDecode, kBatchTC, kPrefillTC };
 Path compute_path(const wisp_layer *L, int T, int K) {
     const long pairs = (long)T * K;
-    if (!prefill_shapes_supported(L->H, L->I)) return Path::kDecode;
+    if (!prefill_shapes_supported(L->H, L->I) || L->compute_class == 1) return Path::kDecode;
     if (pairs >= kPrefillMinPairs) return Path::kPrefillTC;
+    if (L->compute_class == 2) return Path::kBatchTC;
     if (pairs >= L->tc_min_pairs) return Path::kBatchTC;
     return Path::kDecode;
 }
@@ -569,13 +574,21 @@ PrefillGroup tc_group(const wisp_layer *L, const void *x, const float *w, void *
     pg.out = reinterpret_cast<__nv_bfloat16 *>(out);
     pg.status = L->d_status;
     pg.wait_ns = L->wait_ns;
-    pg.ready = L->d_ready;
+    pg.ready = L->d_ready ? L->d_ready + (size_t)L->ready_parity * kBatchReadyWords : nullptr;
     return pg;
+}
+
+// The other counter half (zeroed by the launch about to use `ready`); flips
+// the parity for the next weight-stationary launch.
+uint32_t *take_ready_next(wisp_layer *L) {
+    if (!L->d_ready) return nullptr;
+    L->ready_parity ^= 1;
+    return L->d_ready + (size_t)L->ready_parity * kBatchReadyWords;
 }
 
 int launch_tc_group(wisp_layer *L, Path path, const PrefillGroup &pg, cudaStream_t stream) {
     if (path == Path::kBatchTC) {
-        const int rc = launch_batch_group(pg, stream);
+        const int rc = launch_batch_group(pg, take_ready_next(L), stream);
         if (!rc) L->launches += kBatchKernelsPerGroup;
         return rc;
     }
@@ -649,11 +662,13 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
     return WISP_OK;
 }
 
-// Resident layers run the tensor-core paths without a host round trip: the
-// pager (one group, slots fixed) leaves the group's expert lists and count on
-// the device, the compute kernels read them there and skip the call if the
-// pager rejected it (the gather kernel then records the pager's status in
-// the sticky word, reported by the next call or synchronize).
+// Resident layers run the tensor-core paths without a host round trip.  Up
+// to 256 pairs the weight-stationary kernel routes the call itself (no pager
+// launch: a resident layer's pager step only counts the forward, which that
+// kernel does).  Larger calls: the pager (one group, slots fixed) leaves the
+// expert lists and count on the device and the GEMM kernels read them there.
+// A rejected call is skipped and its status lands in the sticky word,
+// reported by the next call or synchronize.
 int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w, const void *ids, int ids64,
                         int T, int K, void *out, cudaStream_t stream) {
     if (T > L->wsT || K > L->wsK) {
@@ -662,11 +677,28 @@ int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w,
         rc = ensure_ws(L, T, K);
         if (rc) return rc;
     }
-    PagerParams p;
-    fill_pager_params(L, p, ids, ids64, T, K, 0, 1);
     // the layer's workspace: after its previous forward, whichever stream that used
     WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));
     WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
+    if (path == Path::kBatchTC) {
+        BatchRoute r{};
+        r.ids = ids;
+        r.ids64 = ids64;
+        r.E = L->E;
+        r.count_forward = 1;
+        r.emap = L->d_emap;
+        r.hdr = L->d_hdr;
+        r.dev_status = L->d_dev_hdr + kHdrStatus;
+        const int nu_bound = (int)std::min<long>(L->E, (long)T * K);
+        const PrefillGroup pg = tc_group(L, x, w, out, 0, 0, T, K, nu_bound, nullptr);
+        int rc = launch_batch_resident(pg, r, take_ready_next(L), stream);
+        if (rc) return rc;
+        L->launches += kBatchKernelsResident;
+        WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
+        return WISP_OK;
+    }
+    PagerParams p;
+    fill_pager_params(L, p, ids, ids64, T, K, 0, 1);
     int rc = launch_pager(p, stream);
     if (rc) return rc;
     ++L->launches;
@@ -1105,6 +1137,10 @@ int wisp_layer_config(wisp_layer *L, int32_t key, int64_t value) {
         case WISP_CFG_TC_MIN_PAIRS:
             if (value < 1) return fail(WISP_ERR_INVALID, "wisp_layer_config: tensor-core threshold below 1 pair");
             L->tc_min_pairs = (int)std::min<int64_t>(value, kPrefillMinPairs);
+            return WISP_OK;
+        case WISP_CFG_COMPUTE_CLASS:
+            if (value < 0 || value > 2) return fail(WISP_ERR_INVALID, "wisp_layer_config: compute class 0, 1 or 2");
+            L->compute_class = (int)value;
             return WISP_OK;
         default:
             return fail(WISP_ERR_INVALID, "wisp_layer_config: unknown key");

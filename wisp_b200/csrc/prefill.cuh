@@ -38,12 +38,35 @@ constexpr int kPrefillKernelsPerGroup = 4;
 int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream);
 
 // Weight-stationary tensor-core path for decode batches (few tokens per
-// expert): gather, one persistent gate-up + down launch, combine (3 kernels).
+// expert, at most kBatchMaxPairs pairs per group).
+constexpr int kBatchTokens = 32;     // token rows per tile (the MMA's N)
+constexpr int kBatchMaxPairs = 256;  // pairs of one call (or group) on this path
+// Per-token-block counters + one abort word, per launch parity.
+constexpr long kBatchReadyWords = kBatchMaxPairs + (kBatchMaxPairs + kBatchTokens - 1) / kBatchTokens + 1;
+
+// A group whose expert lists come from the pager (paged layers): gather,
+// one persistent gate-up + down launch, combine (3 kernels).  `p.ready` is
+// this launch's counter half, `ready_next` the other half (zeroed here for
+// the next launch).
 constexpr int kBatchKernelsPerGroup = 3;
-constexpr int kBatchTokens = 32;  // token rows per tile (the MMA's N)
-// Per-token-block counters (+ one abort word) the path needs for a group of
-// `npairs` pairs over at most `nu` experts.
-inline long batch_ready_words(long npairs, long nu) { return nu + (npairs + kBatchTokens - 1) / kBatchTokens + 1; }
-int launch_batch_group(const PrefillGroup &p, cudaStream_t stream);
+int launch_batch_group(const PrefillGroup &p, uint32_t *ready_next, cudaStream_t stream);
+
+// A whole call of a resident layer with no pager launch: the persistent
+// kernel routes the pairs itself (counting sort by expert in every CTA,
+// ascending pair order within an expert), gathers the hidden rows its tiles
+// read, counts the forward in the pager counters (forward, groups, unique
+// experts), then runs gate-up and down; the combine follows as a
+// programmatic dependent launch (2 kernels).  A routed id outside [0, E)
+// stops the call before any counter changes, records WISP_ERR_BAD_EXPERT in
+// the sticky word and in *dev_status (the combine then leaves out alone).
+struct BatchRoute {
+    const void *ids;
+    int ids64, E, count_forward;
+    const int32_t *emap;   // [E] slot of each expert
+    int64_t *hdr;          // pager counters: [1] forward, [5] groups, [6] unique experts
+    int32_t *dev_status;   // this call's routing status (device)
+};
+constexpr int kBatchKernelsResident = 2;
+int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, uint32_t *ready_next, cudaStream_t stream);
 
 }  // namespace wisp

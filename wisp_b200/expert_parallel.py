@@ -12,7 +12,12 @@ memory and pages only those into its own HBM slots.  A forward:
 3. runs the owner's paged layer on the rows it received, one expert per row
    (``top_k`` 1): the pager sees the received rows in (source rank, pair)
    order, so a rank's slot maps and hit/miss sequence are those of a one-GPU
-   layer over its shard fed that sequence;
+   layer over its shard fed that sequence.  The rows of each source are
+   computed in the numeric class (CUDA-core or tensor-core kernels) that a
+   one-GPU call of that source's size would use: the counts exchange carries
+   every rank's pair count, and the owner forces that class for the call
+   (sources of both classes: one call per run of sources of one class, so
+   the pager then sees that many calls);
 4. returns the weighted rows to their source and sums them over k in routing
    order (``wisp_ep_combine``).
 
@@ -44,6 +49,7 @@ class DispatchPlan:
     counts_dev: torch.Tensor    # [world + 1] int64: rows per owner, then bad ids
     send_counts: list[int] | None = None
     recv_counts: list[int] | None = None
+    src_pairs: list[int] | None = None   # every source rank's (token, k) pair count
 
 
 class EPMoELayer:
@@ -105,15 +111,18 @@ class EPMoELayer:
             "wisp_ep_dispatch")
 
     def exchange_counts(self, plan: DispatchPlan) -> None:
-        """All-to-all of (rows for you, ids out of range here); one host read."""
+        """All-to-all of (rows for you, ids out of range here, this rank's
+        pair count); one host read."""
         n = plan.counts_dev[: self.world]
         bad = plan.counts_dev[self.world:].expand(self.world)
-        send = torch.stack([n, bad], dim=1).contiguous()
+        pairs = torch.full_like(n, plan.num_tokens * plan.top_k)
+        send = torch.stack([n, bad, pairs], dim=1).contiguous()
         recv = torch.empty_like(send)
         dist.all_to_all_single(recv, send, group=self.group)
         host = torch.cat([send, recv]).cpu().tolist()
         plan.send_counts = [int(r[0]) for r in host[: self.world]]
         plan.recv_counts = [int(r[0]) for r in host[self.world:]]
+        plan.src_pairs = [int(r[2]) for r in host[self.world:]]
         if any(int(r[1]) for r in host[self.world:]):  # (every rank's flag, this one's included)
             raise _lib.WispError(_lib.WISP_ERR_BAD_EXPERT,
                                  f"wisp: a rank routed an expert id outside [0, {self.num_experts})")
@@ -128,14 +137,37 @@ class EPMoELayer:
                                group=self.group)
         return recv_x, recv_meta
 
-    def compute(self, recv_x: torch.Tensor, recv_meta: torch.Tensor) -> torch.Tensor:
-        """This rank's experts on the rows it received (one expert per row)."""
+    def compute(self, recv_x: torch.Tensor, recv_meta: torch.Tensor, recv_counts: list[int] | None = None,
+                src_pairs: list[int] | None = None) -> torch.Tensor:
+        """This rank's experts on the rows it received (one expert per row),
+        each source's rows in the numeric class of a one-GPU call of that
+        source's size (``recv_counts`` / ``src_pairs`` per source rank; without
+        them the class follows the received row count)."""
         R = int(recv_x.shape[0])
         recv_y = torch.empty_like(recv_x)
-        if R:
-            w = recv_meta.view(torch.float32)[:, 1:2]
-            ids = recv_meta[:, 0:1]
+        if not R:
+            return recv_y
+        w = recv_meta.view(torch.float32)[:, 1:2]
+        ids = recv_meta[:, 0:1]
+        classify = getattr(self.local, "compute_class", None)
+        if classify is None or recv_counts is None or src_pairs is None:
             self.local.forward(recv_x, w, ids, out=recv_y)
+            return recv_y
+        runs = []  # [class, first row, rows]: consecutive sources of one class
+        row = 0
+        for cnt, pairs in zip(recv_counts, src_pairs):
+            cls = classify(int(pairs))
+            if cnt and runs and runs[-1][0] == cls:
+                runs[-1][2] += cnt
+            elif cnt:
+                runs.append([cls, row, cnt])
+            row += cnt
+        try:
+            for cls, r0, n in runs:
+                self.local.configure(compute_class=cls)
+                self.local.forward(recv_x[r0:r0 + n], w[r0:r0 + n], ids[r0:r0 + n], out=recv_y[r0:r0 + n])
+        finally:
+            self.local.configure(compute_class="auto")
         return recv_y
 
     def exchange_back(self, plan: DispatchPlan, recv_y: torch.Tensor) -> torch.Tensor:
@@ -163,7 +195,7 @@ class EPMoELayer:
         plan = self.begin(x, topk_weights, topk_ids)
         self.exchange_counts(plan)
         recv_x, recv_meta = self.exchange_rows(plan)
-        recv_y = self.compute(recv_x, recv_meta)
+        recv_y = self.compute(recv_x, recv_meta, plan.recv_counts, plan.src_pairs)
         back = self.exchange_back(plan, recv_y)
         return self.finish(plan, back, out)
 

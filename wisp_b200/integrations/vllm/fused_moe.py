@@ -133,6 +133,7 @@ class WispMoEState:
             "wisp_layer_create")
         self._h = handle
         self._b13, self._b2 = b13, b2
+        self.tc_min_pairs = _lib.TC_MIN_PAIRS_DEFAULT
         self.last_unique_experts: set[int] = set()
         self.stats_pred_hits = 0
         self.stats_pred_total = 0
@@ -299,8 +300,17 @@ class WispMoEState:
         return {"groups": info[0], "misses": info[1], "pagein_bytes": info[2],
                 "unique_experts": info[3], "kernel_launches": n.value}
 
+    def compute_class(self, pairs: int) -> str:
+        """``"tc"`` when a call of ``pairs`` (token, k) pairs runs its expert
+        compute on the tensor cores, else ``"cuda"`` (the library's rule)."""
+        h, i = self.hidden_size, self.intermediate_size
+        if not (h > 0 and i > 0 and h % 256 == 0 and i % 128 == 0):
+            return "cuda"
+        return "tc" if pairs >= min(self.tc_min_pairs, _lib.PREFILL_MIN_PAIRS) else "cuda"
+
     def configure(self, *, asynchronous: bool | None = None, wait_ns: int | None = None,
-                  drop_pageins: int | None = None, tc_min_pairs: int | None = None) -> None:
+                  drop_pageins: int | None = None, tc_min_pairs: int | None = None,
+                  compute_class: str | None = None) -> None:
         """Runtime knobs of the native layer (see ``wisp_layer_config``).
 
         ``asynchronous``: the single-launch forward (default for resident
@@ -308,12 +318,18 @@ class WispMoEState:
         paged single-launch forward waits inside its kernel for page-in copies
         a host thread issues after the launch, so it suits only callers that
         queue no other device work while it pages in.  ``tc_min_pairs``: calls
-        of at least this many (token, k) pairs compute on the tensor cores."""
+        of at least this many (token, k) pairs compute on the tensor cores.
+        ``compute_class``: ``"auto"`` (by call size), ``"cuda"`` or ``"tc"``
+        for every call until changed."""
         L = _lib.lib()
+        cls = None if compute_class is None else {"auto": 0, "cuda": 1, "tc": 2}[compute_class]
         for key, val in ((_lib.CFG_ASYNC, asynchronous), (_lib.CFG_WAIT_NS, wait_ns),
-                         (_lib.CFG_DROP_PAGEINS, drop_pageins), (_lib.CFG_TC_MIN_PAIRS, tc_min_pairs)):
+                         (_lib.CFG_DROP_PAGEINS, drop_pageins), (_lib.CFG_TC_MIN_PAIRS, tc_min_pairs),
+                         (_lib.CFG_COMPUTE_CLASS, cls)):
             if val is not None:
                 _lib.check(L.wisp_layer_config(self._h, key, int(val)), "configure")
+        if tc_min_pairs is not None:
+            self.tc_min_pairs = int(tc_min_pairs)
 
 
 # ---------------------------------------------------------------------------
