@@ -168,16 +168,16 @@ def profile_traffic(name: str):
     return None
 
 
-def dominant_kernel(batch: int) -> str:
+def dominant_kernel(batch: int, tc_min_pairs: int) -> str:
     """The kernel that streams the expert weights in a resident forward of
-    ``batch`` tokens: the one-launch CUDA-core forward below the library's
+    ``batch`` tokens: the one-launch CUDA-core forward below the layer's
     tensor-core threshold, the weight-stationary tcgen05 kernel from it to 256
     pairs, the token-major GEMMs above."""
     from wisp_b200 import _lib
     pairs = batch * SHAPE.top_k
     if pairs >= _lib.PREFILL_MIN_PAIRS:
         return "gateup_gemm_kernel+down_gemm_kernel"
-    return "batch_moe_kernel" if pairs >= _lib.TC_MIN_PAIRS_DEFAULT else "forward_kernel"
+    return "batch_moe_kernel" if pairs >= tc_min_pairs else "forward_kernel"
 
 
 def algorithmic_bytes(unique_experts: int, tokens: int, launches: int) -> int:
@@ -440,11 +440,13 @@ def resident_phase(args, masters, dev, hbm_peak, batch):
     launches = sum(t1["kernel_launches"] - t0["kernel_launches"] for t0, t1 in zip(tel0, tel1))
     nbytes = algorithmic_bytes(unique, B * L * args.steps, launches)
     gbs = nbytes / (ms * 1e-3) / 1e9
+    tc_min_pairs = states[0].tc_min_pairs
     for st in states:
         st.close()
     torch.cuda.empty_cache()
     forwards = args.steps * L
-    return {"layers": L, "batch": B, "kernel": dominant_kernel(B),
+    return {"layers": L, "batch": B, "kernel": dominant_kernel(B, tc_min_pairs),
+            "tc_min_pairs": tc_min_pairs,
             "tok_s_per_layer_stack": B * args.steps / (ms * 1e-3),
             "us_per_forward": ms * 1e3 / forwards, "launches": launches,
             "launches_per_forward": launches / forwards,

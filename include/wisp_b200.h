@@ -152,14 +152,18 @@ WISP_API int wisp_layer_sync(wisp_layer *layer);
  * behind that work until the wait limit), WISP_CFG_WAIT_NS (limit of
  * one device-side wait, default 10 s), WISP_CFG_DROP_PAGEINS (test fault: the
  * host silently skips the next n page-ins of this layer),
- * WISP_CFG_TRACE_BUFFER (debug: device address of a uint64 buffer of
- * 8 + 4 * grid words that the forward kernel fills with %globaltimer
- * milestones; 0 = off), WISP_CFG_TC_MIN_PAIRS (calls of at least this many
+ * WISP_CFG_TRACE_BUFFER (debug: device address of a uint64 buffer that
+ * the one-launch forward kernel (8 + 4096 + 16 * warps of the grid words,
+ * at most 32520 on 148 SMs) and the weight-stationary tensor-core kernel
+ * (8 + 8 * grid words) fill with %globaltimer milestones; 0 = off), WISP_CFG_TC_MIN_PAIRS (calls of at least this many
  * (token, k) pairs run their expert compute on the tcgen05 tensor cores --
  * weight-stationary tiles up to 256 pairs, token-major GEMMs above -- where
  * hidden % 256 == 0 and inter % 128 == 0; smaller calls on the CUDA-core
  * decode kernels.  The choice depends on the call size only, so outputs stay
- * byte-identical across caps and modes; default 64, capped at 257),
+ * byte-identical across caps and modes; default: the smallest call whose
+ * weight-stationary tiles, (I / 128 + H / 256) per pair at most, could fill
+ * the GPU twice over -- 22 pairs at Qwen3-30B-A3B shapes on 148 SMs;
+ * capped at 257),
  * WISP_CFG_COMPUTE_CLASS (0: by call size as above, the default; 1: the
  * CUDA-core kernels at any size; 2: the tensor cores at any size.  The two
  * tensor-core paths give identical bytes, the CUDA-core kernels differ in
@@ -176,6 +180,9 @@ enum wisp_config_key {
     WISP_CFG_COMPUTE_CLASS = 7
 };
 WISP_API int wisp_layer_config(wisp_layer *layer, int32_t key, int64_t value);
+/* Current value of a tunable (WISP_CFG_ASYNC, _WAIT_NS, _TC_MIN_PAIRS,
+ * _COMPUTE_CLASS); no counterpart in the reference. */
+WISP_API int wisp_layer_query(wisp_layer *layer, int32_t key, int64_t *value);
 
 /*
  * Expert compute from slot scratch that allocates nothing (this entry point

@@ -31,8 +31,8 @@ def main():
     gr = torch.Generator().manual_seed(100 + rank)
     ok = 1
     for step in range(5):
-        # call sizes on both sides of the tensor-core threshold (64 pairs), and mixed
-        T = (20 if rank == 0 else 8) if step % 2 else 16
+        # call sizes on both sides of the tensor-core threshold (74 pairs here), and mixed
+        T = (20 if rank == 0 else 8) if step % 2 else 24
         w, ids = wl.softmax_topk(torch.randn(T, E, generator=gr), K)
         x = torch.randn(T, H, generator=gr).to(torch.bfloat16).to(dev)
         out = layer.forward(x, w.to(dev), ids.to(dev))

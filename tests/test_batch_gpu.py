@@ -5,10 +5,10 @@ the same bounds as the prefill path (mean-rel <= 1e-3; per element
 bf16 values may each round the other way with another fp32 accumulation
 order), byte identity across caps, modes and slot placements, agreement with
 the token-major GEMMs on the same pairs, the pager state unchanged by the
-path, the kernel count (resident: the persistent kernel, which routes the
-call itself and counts the forward, and the combine, with no pager launch and
-no host round trip; paged: pager + gather, persistent kernel, combine per
-group), the threshold knob, and a routed id out of range reported at
+path, the kernel count (resident: one persistent kernel that routes the call
+itself, counts the forward and combines, with no pager launch and no host
+round trip; paged: pager + gather and the persistent kernel per group), the
+threshold knob, and a routed id out of range reported at
 synchronize with no counter changed."""
 import pytest
 import torch
@@ -39,7 +39,8 @@ def assert_parity(out, x, w13, w2, w, ids):
 
 @pytest.mark.parametrize("E,H,I,T,K,cap,mode", [
     (128, 2048, 768, 16, 8, 128, "resident"),   # Qwen3-30B-A3B decode, batch 16
-    (128, 2048, 768, 8, 8, 128, "resident"),    # batch 8 (64 pairs: the default threshold)
+    (128, 2048, 768, 8, 8, 128, "resident"),    # batch 8 (64 pairs)
+    (128, 2048, 768, 3, 8, 128, "resident"),    # batch 3 (24 pairs, above the default 22)
     (128, 2048, 768, 16, 8, 40, "paged"),       # paged, several groups
     (8, 4096, 1536, 32, 2, 8, "resident"),      # Qwen3-235B hidden/inter, top-2, 8 tokens/expert
     (16, 256, 128, 64, 4, 16, "resident"),      # small shapes, > 32 pairs per expert (several token blocks)
@@ -81,10 +82,24 @@ def test_batch_agrees_with_token_major_gemm():
     st.close()
 
 
+def test_default_threshold_follows_the_expert_shape():
+    """Default: the smallest call whose tiles (I/128 + H/256 per pair) could
+    fill the GPU twice over; the same for every E (expert-parallel shards)."""
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    for E, H, I in ((128, 2048, 768), (16, 2048, 768), (16, 512, 256), (4, 4096, 1536)):
+        w13 = torch.zeros(E, 2 * I, H, dtype=torch.bfloat16)
+        w2 = torch.zeros(E, H, I, dtype=torch.bfloat16)
+        st = state(w13, w2, E, "paged")
+        per = I // 128 + H // 256
+        assert st.tc_min_pairs == min(max(-(-2 * sms // per), 1), 257), (E, H, I)
+        st.close()
+
+
 def test_batch_pager_state_and_kernel_count():
     E, H, I, T, K, cap = 32, 256, 128, 20, 4, 10
     w13, w2, x, _, _ = rand_case(E, H, I, T, K, seed=29)
     st = state(w13, w2, cap)
+    st.configure(tc_min_pairs=1)
     oracle = PagerOracle(E, cap)
     for step in range(3):
         g = torch.Generator().manual_seed(200 + step)
@@ -94,34 +109,36 @@ def test_batch_pager_state_and_kernel_count():
         groups, _, _ = forward_pager(oracle, ids.numpy())
         tel = st.telemetry()
         assert tel["groups"] - g0 == len(groups)
-        assert tel["kernel_launches"] - l0 == 1 + 3 * len(groups)
+        assert tel["kernel_launches"] - l0 == 1 + 2 * len(groups)
         s2e, tick, clock, stats = st._read()
         assert s2e == oracle.slot_to_expert and tick == oracle.lru_tick and clock == oracle.lru_clock
         assert stats == oracle.stats()
         assert_parity(out, x, w13, w2, w, ids)
     st.close()
     res = state(w13, w2, E, "resident")
+    res.configure(tc_min_pairs=1)
     l0 = res.telemetry()["kernel_launches"]
     res.forward(x.to(DEV), w.to(DEV), ids.to(DEV))
     res.synchronize()
     tel = res.telemetry()
-    assert tel["kernel_launches"] - l0 == 2
+    assert tel["kernel_launches"] - l0 == 1
     assert res.stats() == [1, 0, 0, 0]
     assert tel["groups"] == 1 and tel["unique_experts"] == len(set(ids.reshape(-1).tolist()))
     res.close()
 
 
 def test_threshold_knob_selects_the_path():
-    E, H, I, T, K = 16, 256, 128, 8, 4   # 32 pairs: CUDA-core kernels by default
+    E, H, I, T, K = 16, 256, 128, 8, 4   # 32 pairs: CUDA-core kernels by default (threshold 148)
     w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=31)
     st = state(w13, w2, E, "resident")
+    assert st.tc_min_pairs > T * K
     l0 = st.telemetry()["kernel_launches"]
     a = fwd(st, x, w, ids)
     assert st.telemetry()["kernel_launches"] - l0 == 1      # one-launch forward
     st.configure(tc_min_pairs=32)
     l0 = st.telemetry()["kernel_launches"]
     b = fwd(st, x, w, ids)
-    assert st.telemetry()["kernel_launches"] - l0 == 2      # routing persistent kernel + combine
+    assert st.telemetry()["kernel_launches"] - l0 == 1      # the routing persistent kernel
     for o in (a, b):
         assert_parity(o, x, w13, w2, w, ids)
     with pytest.raises(_lib.WispError):
@@ -133,6 +150,7 @@ def test_batch_bad_expert_reported_at_sync_then_recovers():
     E, H, I, T, K = 16, 256, 128, 16, 4
     w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=37)
     st = state(w13, w2, E, "resident")
+    st.configure(tc_min_pairs=1)
     bad = ids.clone()
     bad[3, 1] = E + 5
     st.forward(x.to(DEV), w.to(DEV), bad.to(torch.int32).to(DEV))

@@ -6,7 +6,7 @@
   byte-identical to the one-GPU layer over all experts, and each paged rank's
   pager state must equal the oracle pager over its shard fed the rows it
   received, in (source rank, pair) order.  Call sizes on either side of the
-  tensor-core threshold (64 pairs), also mixed across ranks: each owner
+  tensor-core threshold (74 pairs at these shapes), also mixed across ranks: each owner
   computes a source's rows in the class of that source's call size.
 * Two real ranks over NCCL (needs two GPUs; skipped otherwise): the same
   byte identity through torch.distributed.
@@ -66,7 +66,7 @@ def emulated_forward(layers, xs, ws, idss):
 @pytest.mark.parametrize("P,cap,mode,K,Ts", [
     (2, 8, "resident", 4, (6, 6)), (2, 3, "paged", 4, (6, 6)), (4, 2, "paged", 4, (6, 6, 6, 6)),
     (4, 4, "resident", 4, (6, 6, 6, 6)),
-    (4, 4, "resident", 8, (8, 8, 8, 8)),      # 64 pairs per source: tensor cores, owners get ~64 rows
+    (4, 4, "resident", 8, (10, 10, 10, 10)),  # 80 pairs per source: tensor cores (threshold 74), owners ~80 rows
     (2, 8, "resident", 8, (12, 3)),           # one source above the threshold, one below
     (2, 8, "paged", 8, (12, 12)),
 ])

@@ -29,7 +29,6 @@ CFG_DROP_PAGEINS = 4
 CFG_TRACE_BUFFER = 5
 CFG_TC_MIN_PAIRS = 6
 CFG_COMPUTE_CLASS = 7
-TC_MIN_PAIRS_DEFAULT = 64   # the library's default tensor-core threshold (pairs)
 PREFILL_MIN_PAIRS = 257     # calls from this size always run on the tensor cores
 
 _c_int32 = ctypes.c_int32
@@ -59,6 +58,7 @@ SIGNATURES = {
     "wisp_get_launch_count": (ctypes.c_int, [_vp, _p64]),
     "wisp_layer_sync": (ctypes.c_int, [_vp]),
     "wisp_layer_config": (ctypes.c_int, [_vp, _c_int32, _c_int64]),
+    "wisp_layer_query": (ctypes.c_int, [_vp, _c_int32, ctypes.POINTER(_c_int64)]),
     "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,
                                                    _c_int32, _c_int32, _c_int32, _c_int32, _vp, _vp]),
     "wisp_ep_dispatch": (ctypes.c_int, [_vp, _vp, _c_int32, _vp, _c_int32, _c_int32, _c_int32, _c_int32,

@@ -21,8 +21,12 @@
 // expert-major pair order, so each weight tile is streamed once per token
 // block, i.e. once per expert for a decode batch.  Gate-up and down share ONE
 // persistent launch: tiles are numbered gate-up first, then down, both in
-// token-block order, and each CTA walks its tiles (t = blockIdx.x,
-// + gridDim.x, ...) in that order.  Before the producer loads a down tile it
+// token-block order, handed out in that order by a per-launch counter: each
+// CTA's producer takes the next index when it starts a tile and passes it to
+// the MMA thread and the epilogue through a small shared-memory ring, so
+// CTAs that drew heavy tiles take fewer (dynamic balance; a down tile's
+// gate-up tiles were always taken earlier, by running CTAs).  Before the
+// producer loads a down tile it
 // waits until the block's gate-up tiles have published their activation rows:
 // every epilogue warp adds 1 to the block's counter after its stores (release
 // at GPU scope, after an async-proxy fence, since the rows are read back by
@@ -37,9 +41,9 @@
 // / u_slot in global memory, X_perm written by the gather kernel) or, for a
 // resident layer's call, from the kernel itself: every CTA sorts the call's
 // (at most 256) pairs by expert in shared memory -- experts ascending, pairs
-// ascending within an expert, slots from the expert map -- and copies the
-// hidden rows of the token blocks of its own gate-up tiles into X_perm before
-// its producer starts (CTAs that share a block write identical bytes).
+// ascending within an expert, slots from the expert map -- copies every
+// gridDim.x-th row of X_perm (its share) and counts itself in; a producer
+// waits for all CTAs' shares before its first gate-up load.
 //
 // Roles per CTA (192 threads, one CTA per SM): warp 0 lane 0 issues the TMA
 // loads of a 6-stage ring (two 128 x 64 weight boxes and one 32 x 64 token
@@ -96,6 +100,9 @@ constexpr int kMaxRouteExperts = 1024;
 static_assert(kTmemCols >= 32 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation: power of two >= 32");
 static_assert(kTN == 32, "the epilogue reads one 32-column TMEM block per accumulator");
 static_assert(3 * kMaxRouteExperts * 4 + kMaxPairs * 4 <= kStages * kStageBytes, "routing scratch fits the ring");
+static_assert(kMaxPairs + (kMaxPairs + kTN - 1) / kTN + 3 == kBatchReadyWords, "counter words");
+constexpr int kTileRing = 4;                      // tile indices handed from the producer to the other roles
+constexpr int kMaxBlocks = kMaxPairs + (kMaxPairs + kTN - 1) / kTN;
 
 struct Args {
     // lists from the pager (route == false)
@@ -114,23 +121,47 @@ struct Args {
     int64_t *hdr;
     int32_t *dev_status;
     // both
-    int H, I;
+    int H, I, Kc, t0;           // Kc: top-k; t0: first token of the group
     const float *topk_w;        // [T * K]
     __nv_bfloat16 *act_perm;    // [npairs][I]
     __nv_bfloat16 *y;           // [T * K][H]
-    uint32_t *ready;            // this launch's counters; [kBatchReadyWords - 1] abort word
+    __nv_bfloat16 *out;         // [T][H]
+    uint32_t *ready;            // this launch's counters: [blocks], gathered CTAs, abort word
     uint32_t *ready_next;       // the other half, zeroed for the next launch
+    uint32_t *done;             // [tokens][H / 256][4] down rows stored, per epilogue warp
+    uint32_t *done_next;        // the other half, zeroed for the next launch
     int *status;
     long long wait_ns;
+    unsigned long long *trace;  // debug: per CTA kTraceWords %globaltimer milestones, or nullptr
 };
+
+// Trace milestones of a CTA (words 8 + kTraceWords * blockIdx.x + i).
+enum { kTrEntry, kTrLists, kTrRoles, kTrFirstLoad, kTrLastLoad, kTrLastMma, kTrEpiDone, kTrExit, kTraceWords };
+__device__ __forceinline__ void trace_at(const unsigned long long *tr, int i) {
+    if (tr) const_cast<unsigned long long *>(tr)[8 + kTraceWords * blockIdx.x + i] = globaltimer_ns();
+}
 
 struct Ring {
     uint64_t full[kStages], empty[kStages];
     uint64_t acc_full[2], acc_empty[2], mma_done;
+    uint64_t tile_full[kTileRing], tile_empty[kTileRing];
+    int tile[kTileRing];  // i-th tile of this CTA at [i % kTileRing]; -1: no more
     uint32_t tmem_base;
     int abort;
     int issued, consumed;
 };
+
+// The MMA thread's and the epilogue warps' i-th tile (bounded wait; -1 when
+// there are no more or the wait gave up).  The epilogue's lane 0 and the MMA
+// thread release the entry.
+__device__ __forceinline__ int next_tile(Ring &R, int i, const Args &g, bool release) {
+    volatile int *abort = &R.abort;
+    const int slot = i % kTileRing;
+    if (!mbar_wait(&R.tile_full[slot], (i / kTileRing) & 1, g.wait_ns, abort)) return -1;
+    const int t = *reinterpret_cast<volatile int *>(&R.tile[slot]);
+    if (release) mbar_arrive(&R.tile_empty[slot]);
+    return t;
+}
 
 // The call's (or group's) experts, their token blocks and pair lists.
 struct Lists {
@@ -139,6 +170,8 @@ struct Lists {
     int first[kMaxPairs + 1];  // first token block of each expert (prefix of block counts)
     int pairs[kMaxPairs];      // routed lists: absolute pair index, expert-major
     int slot[kMaxPairs];       // routed lists: slot of each expert
+    int rows[kMaxBlocks];      // rows of each token block
+    int order[kMaxBlocks];     // blocks by rows, most first (ties: lower block first)
 };
 
 // Token block b -> expert u, first list position q0, rows.
@@ -161,10 +194,13 @@ struct Tile {
     int b;     // token block
     int col;   // 128-row block of I (gate-up) or 256-row block of H (down)
 };
-__device__ __forceinline__ Tile tile_at(int t, int ngu, int cj, int ch) {
-    if (t < ngu) return Tile{0, t / cj, t % cj};
+// Tiles in block order (blocks with the most rows first): the epilogue
+// work of a tile grows with its rows and the combines of a token fall to its
+// last tile, so the last tiles handed out are the lightest.
+__device__ __forceinline__ Tile tile_at(const Lists &L, int t, int ngu, int cj, int ch) {
+    if (t < ngu) return Tile{0, L.order[t / cj], t % cj};
     t -= ngu;
-    return Tile{1, t / ch, t % ch};
+    return Tile{1, L.order[t / ch], t % ch};
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -183,17 +219,27 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
 __device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+constexpr int kGatheredWord = kBatchReadyWords - 3;
+constexpr int kSchedWord = kBatchReadyWords - 2;
+constexpr int kAbortWord = kBatchReadyWords - 1;
 
 __device__ __forceinline__ void give_up(Ring &R, const Args &g) {
     R.abort = 1;
     if (g.status) *reinterpret_cast<volatile int *>(g.status) = WISP_ERR_TIMEOUT;
-    atomicExch(g.ready + kBatchReadyWords - 1, 1u);  // ends the other CTAs' waits
+    atomicExch(g.ready + kAbortWord, 1u);  // ends the other CTAs' waits
 }
 
-// Producer wait for a down tile: the block's activation rows are published.
-__device__ __forceinline__ bool wait_ready(const Args &g, int b, uint32_t need, volatile int *abort) {
-    const uint32_t *word = g.ready + b;
-    const volatile uint32_t *abort_all = g.ready + kBatchReadyWords - 1;
+// Producer wait on a counter word of this launch (a down tile's block: its
+// activation rows published; kGatheredWord: every CTA's X_perm rows).
+__device__ __forceinline__ bool wait_ready(const Args &g, int word_index, uint32_t need, volatile int *abort) {
+    const uint32_t *word = g.ready + word_index;
+    const volatile uint32_t *abort_all = g.ready + kAbortWord;
     if (ld_acquire_gpu(word) < need) {
         const unsigned long long t0 = globaltimer_ns();
         while (ld_acquire_gpu(word) < need) {
@@ -211,6 +257,54 @@ __device__ __forceinline__ unsigned char *align1024(unsigned char *p) {
     return p + ((1024u - (a & 1023u)) & 1023u);
 }
 
+// After an epilogue warp stored its rows h and h + 128 of a down tile's
+// pairs: count the warp in for each of those pairs' tokens (lane n takes row
+// n, all rows at once, acquire-release at GPU scope after a warp barrier, so
+// the other lanes' stores are released too); the warp that brings a (token,
+// 256-row block, quarter) counter to top-k holds the last of the token's
+// weighted rows there and writes out[t] = the routing-order fp32 sum of the
+// bf16 rows y[t * K + k], rounded to bf16 (the combine kernel's
+// arithmetic), loading up to 8 rows at a time past L1 before summing them.
+__device__ __forceinline__ void combine_rows(const Args &g, const int32_t *pairs, int q0, int rows, int col,
+                                             int quarter, int lane, int h) {
+    const int K = g.Kc, H = g.H, ch = H / kDownRows;
+    __syncwarp();
+    int t = 0;
+    bool last = false;
+    if (lane < rows) {
+        t = pairs[q0 + lane] / K;
+        last = atom_add_acq_rel_gpu(g.done + ((size_t)(t - g.t0) * ch + col) * 4 + quarter, 1u) + 1 == (uint32_t)K;
+    }
+    unsigned lm = __ballot_sync(0xffffffffu, last);
+    __syncwarp();
+    while (lm) {
+        const int n = __ffs(lm) - 1;
+        lm &= lm - 1;
+        const int tt = __shfl_sync(0xffffffffu, t, n);
+        const unsigned short *row = reinterpret_cast<const unsigned short *>(g.y + (size_t)tt * K * H + h);
+        float a0 = 0.f, a1 = 0.f;
+        for (int k0 = 0; k0 < K; k0 += 8) {
+            unsigned short v0[8], v1[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (k0 + j < K) {
+                    v0[j] = __ldcg(row + (size_t)(k0 + j) * H);
+                    v1[j] = __ldcg(row + (size_t)(k0 + j) * H + kWM);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (k0 + j < K) {
+                    a0 += bf16lo((uint32_t)v0[j]);
+                    a1 += bf16lo((uint32_t)v1[j]);
+                }
+            }
+        }
+        g.out[(size_t)tt * H + h] = __float2bfloat16_rn(a0);
+        g.out[(size_t)tt * H + h + kWM] = __float2bfloat16_rn(a1);
+    }
+}
+
 // Every CTA: the call's pairs sorted by expert (experts ascending, pairs
 // ascending within one), with the ring as scratch.  Sets L.bad on an id
 // outside [0, E).
@@ -219,8 +313,12 @@ __device__ void route_pairs(const Args &g, Lists &L, unsigned char *scratch) {
     const int E = g.E, P = g.T * g.K;
     int *cnt = reinterpret_cast<int *>(scratch);  // [E] pairs per expert
     int *base = cnt + kMaxRouteExperts;           // [E] next list position of each expert
-    int *ids = base + kMaxRouteExperts;           // [P]
-    for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+    int *emap = base + kMaxRouteExperts;          // [E] slot of each expert
+    int *ids = emap + kMaxRouteExperts;           // [P]
+    for (int e = tid; e < E; e += blockDim.x) {
+        cnt[e] = 0;
+        emap[e] = g.emap[e];
+    }
     __syncthreads();
     bool bad = false;
     for (int p = tid; p < P; p += blockDim.x) {
@@ -258,7 +356,7 @@ __device__ void route_pairs(const Args &g, Lists &L, unsigned char *scratch) {
             const int c = cnt[e];
             if (c > 0) {
                 L.off[u] = at;
-                L.slot[u] = g.emap[e];
+                L.slot[u] = emap[e];
                 base[e] = at;
                 ++u;
                 at += c;
@@ -294,12 +392,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char *stages = align1024(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = g.H, I = g.I;
+    if (threadIdx.x == 0) trace_at(g.trace, kTrEntry);
 
     // the next launch's counters
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kBatchReadyWords; i += gridDim.x * blockDim.x)
-        g.ready_next[i] = 0;
-    // the combine may be scheduled now (it waits for this grid's completion)
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    {
+        const int gtid = blockIdx.x * blockDim.x + threadIdx.x, gstride = gridDim.x * blockDim.x;
+        for (int i = gtid; i < kBatchReadyWords; i += gstride) g.ready_next[i] = 0;
+        const int ndone = batch_done_words(g.H);
+        for (int i = gtid; i < ndone; i += gstride) g.done_next[i] = 0;
+    }
 
     // ---- the expert lists ----------------------------------------------------------
     const int32_t *pairs;
@@ -323,14 +424,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         pairs = g.u_pairs;
         __syncthreads();
     }
-    if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int e = 0; e < L.nu; ++e) {
+    if (warp == 0) {
+        // token blocks per expert: prefix over experts in contiguous chunks per lane
+        const int nu = L.nu, chunk = (nu + 31) / 32, e0 = min(nu, lane * chunk), e1 = min(nu, e0 + chunk);
+        int nb = 0;
+        for (int e = e0; e < e1; ++e) nb += (L.off[e + 1] - L.off[e] + kTN - 1) / kTN;
+        int inc = nb;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += v;
+        }
+        int acc = inc - nb;
+        for (int e = e0; e < e1; ++e) {
             L.first[e] = acc;
             acc += (L.off[e + 1] - L.off[e] + kTN - 1) / kTN;
         }
-        L.first[L.nu] = acc;
-        L.nblocks = acc;
+        if (lane == 31) {
+            L.first[nu] = inc;
+            L.nblocks = inc;
+        }
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < L.nblocks; b += blockDim.x) {
+        int u, q0, rows;
+        block_of(L, b, u, q0, rows);
+        L.rows[b] = rows;
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < L.nblocks; b += blockDim.x) {
+        const int rb = L.rows[b];
+        int rank = 0;
+        for (int c = 0; c < L.nblocks; ++c) {
+            const int rc = L.rows[c];
+            rank += (rc > rb) || (rc == rb && c < b);
+        }
+        L.order[rank] = b;
+    }
+    if (threadIdx.x == 0) {
         R.abort = 0;
         R.issued = R.consumed = 0;
         if (g.route && blockIdx.x == 0) {
@@ -342,24 +473,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0) trace_at(g.trace, kTrLists);
     const int cj = I / kWM, ch = H / kDownRows;
     const int ngu = L.nblocks * cj;
     const int ntiles = ngu + L.nblocks * ch;
-    if ((int)blockIdx.x >= ntiles) return;
-
     if (g.route) {
-        // hidden rows of this CTA's gate-up blocks into X_perm (read back by TMA)
-        const int H8 = H / 8;
-        for (int t = blockIdx.x; t < ngu; t += gridDim.x) {
-            int u, q0, rows;
-            block_of(L, t / cj, u, q0, rows);
-            for (int i = threadIdx.x; i < rows * H8; i += blockDim.x) {
-                const int q = q0 + i / H8, c = i % H8;
-                g.x_perm[(size_t)q * H8 + c] = g.x[(size_t)(L.pairs[q] / g.K) * H8 + c];
-            }
+        // this CTA's share of X_perm: rows blockIdx.x, + gridDim.x, ... (read back
+        // by TMA in every CTA), then count the CTA in
+        const int H8 = H / 8, P = g.T * g.K;
+        for (int q = blockIdx.x; q < P; q += gridDim.x) {
+            const uint4 *src = g.x + (size_t)(L.pairs[q] / g.K) * H8;
+            uint4 *dst = g.x_perm + (size_t)q * H8;
+            for (int c = threadIdx.x; c < H8; c += blockDim.x) dst[c] = src[c];
         }
         fence_proxy_async_global();
+        __syncthreads();
+        if (threadIdx.x == 0) red_release_gpu_add(g.ready + kGatheredWord, 1u);
     }
+    if ((int)blockIdx.x >= ntiles) return;
     __syncthreads();  // the ring is no longer scratch
 
     if (threadIdx.x == 0) {
@@ -372,6 +503,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&R.acc_empty[b], kEpiThreads);
         }
         mbar_init(&R.mma_done, 1);
+        for (int k = 0; k < kTileRing; ++k) {
+            mbar_init(&R.tile_full[k], 1);
+            mbar_init(&R.tile_empty[k], 1 + kEpiWarps);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -379,6 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (threadIdx.x == 0) trace_at(g.trace, kTrRoles);
     volatile int *abort = &R.abort;
     const uint32_t need = (uint32_t)(kEpiWarps * cj);
 
@@ -387,8 +523,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint64_t once = policy_evict_first();  // each weight tile is read once
             int kstep = 0;
-            for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-                const Tile tl = tile_at(t, ngu, cj, ch);
+            bool gathered = false;
+            for (int i = 0;; ++i) {
+                const int ts = i % kTileRing;
+                if (i >= kTileRing &&
+                    !mbar_wait(&R.tile_empty[ts], ((i / kTileRing) - 1) & 1, g.wait_ns, abort)) {
+                    give_up(R, g);
+                    break;
+                }
+                int t = (int)atomicAdd(g.ready + kSchedWord, 1u);
+                if (t >= ntiles) t = -1;
+                R.tile[ts] = t;
+                mbar_arrive(&R.tile_full[ts]);
+                if (t < 0) break;
+                const Tile tl = tile_at(L, t, ngu, cj, ch);
                 int u, q0, rows;
                 block_of(L, tl.b, u, q0, rows);
                 const int slot = L.slot[u];
@@ -400,6 +548,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     a0 = slot * 2 * I + tl.col * kWM;
                     a1 = a0 + I;
                     kbc = H / kBK;
+                    if (g.route && !gathered) {
+                        if (!wait_ready(g, kGatheredWord, gridDim.x, abort)) {
+                            give_up(R, g);
+                            break;
+                        }
+                        gathered = true;
+                    }
                 } else {
                     mw = &map_w2;
                     mt = &map_act;
@@ -424,6 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_2d_hint(st, mw, kb * kBK, a0, &R.full[s], once);
                     tma_load_2d_hint(st + kWBoxBytes, mw, kb * kBK, a1, &R.full[s], once);
                     tma_load_2d(st + 2 * kWBoxBytes, mt, kb * kBK, q0, &R.full[s]);
+                    if (kstep == 0) trace_at(g.trace, kTrFirstLoad);
                     R.issued = kstep + 1;
                 }
                 if (!ok) {
@@ -431,13 +587,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
             }
+            trace_at(g.trace, kTrLastLoad);
         }
     } else if (warp == 1) {
         // ---- MMA issuer -------------------------------------------------------------
         if (lane == 0) {
             const uint32_t idesc = gemm::idesc_bf16_f32(kWM, kTN);
-            int kstep = 0, i = 0;
-            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+            int kstep = 0;
+            for (int i = 0;; ++i) {
+                const int t = next_tile(R, i, g, true);
+                if (t < 0) break;
                 const int kbc = (t < ngu ? H : I) / kBK;
                 const int b = i & 1;
                 if (i >= 2 && !mbar_wait(&R.acc_empty[b], ((i / 2) - 1) & 1, g.wait_ns, abort)) {
@@ -473,16 +632,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_commit(&R.acc_full[b]);
             }
             umma_commit(&R.mma_done);  // every MMA issued (also after an abort)
+            trace_at(g.trace, kTrLastMma);
         }
     } else {
         // ---- epilogue (warps 2..5) ----------------------------------------------------
         const int quarter = warp & 3, r = quarter * 32 + lane;
-        int i = 0;
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        for (int i = 0;; ++i) {
+            int t = next_tile(R, i, g, false);
+            t = __shfl_sync(0xffffffffu, t, 0);
+            __syncwarp();
+            if (lane == 0 && t >= 0) mbar_arrive(&R.tile_empty[i % kTileRing]);
+            if (t < 0) break;
             const bool ok = mbar_wait(&R.acc_full[i & 1], (i / 2) & 1, g.wait_ns, abort) && !*abort;
             if (!__all_sync(0xffffffffu, ok)) break;  // uniform: the TMEM loads are .sync.aligned
             tc_fence_after();
-            const Tile tl = tile_at(t, ngu, cj, ch);
+            const Tile tl = tile_at(L, t, ngu, cj, ch);
             int u, q0, rows;
             block_of(L, tl.b, u, q0, rows);
             const uint32_t tbase = R.tmem_base + (i & 1) * kAccCols + ((uint32_t)(quarter * 32) << 16);
@@ -503,10 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fence_proxy_async_global();
                 __syncwarp();
-                if (lane == 0) {
-                    __threadfence();
-                    red_release_gpu_add(g.ready + tl.b, 1u);
-                }
+                if (lane == 0) red_release_gpu_add(g.ready + tl.b, 1u);
             } else {
                 const int h = tl.col * kDownRows + r;
 #pragma unroll
@@ -519,8 +680,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         dst[kWM] = __float2bfloat16_rn(__uint_as_float(d1[n]) * wp);
                     }
                 }
+                combine_rows(g, pairs, q0, rows, tl.col, quarter, lane, h);
             }
         }
+        if (warp == 2 && lane == 0) trace_at(g.trace, kTrEpiDone);
     }
 
     // ---- teardown ----------------------------------------------------------------------
@@ -536,6 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 0) tmem_dealloc(R.tmem_base, kTmemCols);
+    if (threadIdx.x == 0) trace_at(g.trace, kTrExit);
 }
 
 // Shared launch of the persistent kernel (cooperative: at most one CTA per
@@ -573,37 +737,44 @@ int launch_kernel(const PrefillGroup &p, const Args &a, long nu_bound, cudaStrea
     return WISP_OK;
 }
 
-int check_group(const PrefillGroup &p, const uint32_t *ready_next) {
+int check_group(const PrefillGroup &p, const BatchCounters &c) {
     if (!prefill_shapes_supported(p.H, p.I))
         return set_error("wisp: tensor-core path needs hidden % 256 == 0 and inter % 128 == 0"), WISP_ERR_UNSUPPORTED;
     if (p.npairs > kMaxPairs)
         return set_error("wisp: weight-stationary path takes at most 256 pairs per call"), WISP_ERR_INVALID;
-    if (!p.ready || !ready_next) return set_error("wisp: batch path without its counters"), WISP_ERR_INVALID;
+    if (!c.ready || !c.ready_next || !c.done || !c.done_next)
+        return set_error("wisp: batch path without its counters"), WISP_ERR_INVALID;
     return WISP_OK;
 }
 
-Args common_args(const PrefillGroup &p, uint32_t *ready_next) {
+Args common_args(const PrefillGroup &p, const BatchCounters &c) {
     Args a{};
     a.H = p.H;
     a.I = p.I;
+    a.Kc = p.K;
+    a.t0 = p.t0;
     a.topk_w = p.topk_w;
     a.act_perm = p.act_perm;
     a.y = p.y;
-    a.ready = p.ready;
-    a.ready_next = ready_next;
+    a.out = p.out;
+    a.ready = c.ready;
+    a.ready_next = c.ready_next;
+    a.done = c.done;
+    a.done_next = c.done_next;
     a.status = p.status;
     a.wait_ns = p.wait_ns;
+    a.trace = p.trace;
     return a;
 }
 
 }  // namespace
 }  // namespace batch
 
-int launch_batch_group(const PrefillGroup &p, uint32_t *ready_next, cudaStream_t stream) {
+int launch_batch_group(const PrefillGroup &p, const BatchCounters &c, cudaStream_t stream) {
     using namespace batch;
-    int rc = check_group(p, ready_next);
+    int rc = check_group(p, c);
     if (rc || p.npairs <= 0 || p.nu <= 0) return rc;
-    Args a = common_args(p, ready_next);
+    Args a = common_args(p, c);
     a.u_off = p.u_off;
     a.u_pairs = p.u_pairs;
     a.u_slot = p.u_slot;
@@ -611,17 +782,16 @@ int launch_batch_group(const PrefillGroup &p, uint32_t *ready_next, cudaStream_t
     a.pager_status = p.pager_status;
     rc = gemm::launch_gather(p, stream);
     if (!rc) rc = launch_kernel(p, a, p.nu, stream);
-    if (!rc) rc = gemm::launch_combine(p, stream, true);
     return rc;
 }
 
-int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, uint32_t *ready_next, cudaStream_t stream) {
+int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, const BatchCounters &c, cudaStream_t stream) {
     using namespace batch;
-    int rc = check_group(p, ready_next);
+    int rc = check_group(p, c);
     if (rc || p.npairs <= 0) return rc;
     if (r.E < 1 || r.E > kMaxRouteExperts)
         return set_error("wisp: in-kernel routing takes at most 1024 experts"), WISP_ERR_INVALID;
-    Args a = common_args(p, ready_next);
+    Args a = common_args(p, c);
     a.route = 1;
     a.ids = r.ids;
     a.ids64 = r.ids64;
@@ -634,11 +804,7 @@ int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, uint32_t *
     a.x_perm = reinterpret_cast<uint4 *>(p.x_perm);
     a.hdr = r.hdr;
     a.dev_status = r.dev_status;
-    PrefillGroup pc = p;
-    pc.pager_status = r.dev_status;  // the combine leaves out alone after a rejected call
-    rc = launch_kernel(p, a, std::min(r.E, p.npairs), stream);
-    if (!rc) rc = gemm::launch_combine(pc, stream, true);
-    return rc;
+    return launch_kernel(p, a, std::min(r.E, p.npairs), stream);
 }
 
 }  // namespace wisp

@@ -245,10 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // out[t] = sum over k in routing order of y[t * K + k], t in [t0, t1).
-// May run as a programmatic dependent launch: waits for the producing grid.
 __global__ void combine_kernel(const uint4 *y, int t0, int t1, int K, int H8, uint4 *out,
                                const int32_t *pager_status) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (pager_status && *reinterpret_cast<const volatile int32_t *>(pager_status) != WISP_OK) return;
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long)(t1 - t0) * H8) return;
@@ -317,20 +315,13 @@ int launch_gather(const PrefillGroup &p, cudaStream_t stream) {
     return WISP_OK;
 }
 
-int launch_combine(const PrefillGroup &p, cudaStream_t stream, bool dependent) {
+int launch_combine(const PrefillGroup &p, cudaStream_t stream) {
     const long n = (long)(p.t1 - p.t0) * (p.H / 8);
     if (n <= 0) return WISP_OK;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)((n + 255) / 256));
-    cfg.blockDim = dim3(256);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = dependent ? 1 : 0;
-    WISP_CUDA_TRY(cudaLaunchKernelEx(&cfg, combine_kernel, reinterpret_cast<const uint4 *>(p.y), p.t0, p.t1, p.K,
-                                     p.H / 8, reinterpret_cast<uint4 *>(p.out), p.pager_status));
+    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const uint4 *>(p.y), p.t0, p.t1, p.K, p.H / 8, reinterpret_cast<uint4 *>(p.out),
+        p.pager_status);
+    WISP_CUDA_TRY(cudaGetLastError());
     return WISP_OK;
 }
 
@@ -387,7 +378,7 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
     WISP_CUDA_TRY(cudaGetLastError());
     down_gemm_kernel<<<grid_dn, kThreads, kSmemBytes, stream>>>(mact, mw2, g);
     WISP_CUDA_TRY(cudaGetLastError());
-    return launch_combine(p, stream, false);
+    return launch_combine(p, stream);
 }
 
 }  // namespace wisp

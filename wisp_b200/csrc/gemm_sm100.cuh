@@ -300,9 +300,8 @@ __device__ __forceinline__ int group_experts(const int32_t *nu_dev, const int32_
 int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 // X_perm rows of the group.
 int launch_gather(const PrefillGroup &p, cudaStream_t stream);
-// out rows [t0, t1) = routing-order sum of the weighted rows y; `dependent`:
-// a programmatic dependent launch of the kernel queued before it.
-int launch_combine(const PrefillGroup &p, cudaStream_t stream, bool dependent);
+// out rows [t0, t1) = routing-order sum of the weighted rows y.
+int launch_combine(const PrefillGroup &p, cudaStream_t stream);
 
 }  // namespace gemm
 }  // namespace wisp

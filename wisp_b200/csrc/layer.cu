@@ -88,11 +88,23 @@ void init_write32() {
 }
 
 constexpr long long kDefaultWaitNs = 10LL * 1000 * 1000 * 1000;
-// Calls of T * k pairs in [kDefaultTcMinPairs, kPrefillMinPairs) run on the
+// Calls of T * k pairs in [tc_min_pairs, kPrefillMinPairs) run on the
 // weight-stationary tensor-core path, larger ones on the token-major GEMMs,
 // smaller ones on the CUDA-core decode kernels.
-constexpr int kDefaultTcMinPairs = 64;
 constexpr int kPrefillMinPairs = 257;
+
+// Default tensor-core threshold of a layer: the smallest call whose
+// weight-stationary tiles -- I / 128 gate-up + H / 256 down per pair at most
+// -- could fill the GPU twice over, so calls of one tile per SM or fewer stay
+// on the CUDA-core kernels, which spread an expert over every SM.  It
+// depends on the expert shape only (not on E), so an expert-parallel shard
+// and a one-GPU layer of the same model choose alike.  (Qwen3-30B-A3B
+// shapes on 148 SMs: 22 pairs; measured crossover between 16 and 24.)
+int default_tc_min_pairs(int H, int I, int sms) {
+    const int per = I / 128 + H / 256;
+    if (per <= 0 || sms <= 0) return kPrefillMinPairs;
+    return std::min(std::max((2 * sms + per - 1) / per, 1), kPrefillMinPairs);
+}
 constexpr int kMbRing = 4;
 
 }  // namespace
@@ -121,8 +133,9 @@ struct wisp_layer {
     __nv_bfloat16 *d_act = nullptr, *d_y = nullptr;
     __nv_bfloat16 *d_xperm = nullptr, *d_actperm = nullptr;  // tensor-core paths: rows, expert-major
     uint32_t *d_ready = nullptr;     // weight-stationary path: per-token-block counters, two halves
-    int ready_parity = 0;            // the half the next weight-stationary launch uses
-    int tc_min_pairs = kDefaultTcMinPairs;  // calls of at least this many pairs run on the tensor cores
+    uint32_t *d_combined = nullptr;  // weight-stationary path: per-token combine counters, two halves
+    int ready_parity = 0;            // the halves the next weight-stationary launch uses
+    int tc_min_pairs = kPrefillMinPairs;  // calls of at least this many pairs run on the tensor cores
     int compute_class = 0;           // 0: by call size; 1: CUDA-core kernels; 2: tensor cores
     int32_t *h_mb = nullptr, *d_mb = nullptr;  // kMbRing mailboxes of mb_words words
     long mb_words = 0;
@@ -331,13 +344,13 @@ void free_ws(wisp_layer *L) {
                     (void *)L->d_grp_nhit, (void *)L->d_u_slot,
                     (void *)L->d_u_gen, (void *)L->d_u_off, (void *)L->d_u_pairs, (void *)L->d_counters,
                     (void *)L->d_dev_hdr, (void *)L->d_act, (void *)L->d_y, (void *)L->d_xperm,
-                    (void *)L->d_actperm, (void *)L->d_ready})
+                    (void *)L->d_actperm, (void *)L->d_ready, (void *)L->d_combined})
         cudaFree(p);
     if (L->h_mb) cudaFreeHost(L->h_mb);
     L->d_slots = L->d_grp_start = L->d_grp_nu = L->d_grp_nhit = L->d_u_slot = L->d_u_gen = L->d_u_off =
         L->d_u_pairs = L->d_counters = L->d_dev_hdr = nullptr;
     L->d_act = L->d_y = L->d_xperm = L->d_actperm = nullptr;
-    L->d_ready = nullptr;
+    L->d_ready = L->d_combined = nullptr;
     L->h_mb = L->d_mb = nullptr;
     L->wsT = -1;
     L->wsK = 0;
@@ -379,6 +392,8 @@ int ensure_ws(wisp_layer *L, int T, int K) {
             WISP_CUDA_TRY(cudaMalloc(&L->d_actperm, sizeof(__nv_bfloat16) * P * I));
             WISP_CUDA_TRY(cudaMalloc(&L->d_ready, sizeof(uint32_t) * 2 * kBatchReadyWords));
             WISP_CUDA_TRY(cudaMemset(L->d_ready, 0, sizeof(uint32_t) * 2 * kBatchReadyWords));
+            WISP_CUDA_TRY(cudaMalloc(&L->d_combined, sizeof(uint32_t) * 2 * batch_done_words(L->H)));
+            WISP_CUDA_TRY(cudaMemset(L->d_combined, 0, sizeof(uint32_t) * 2 * batch_done_words(L->H)));
             L->ready_parity = 0;
         }
     }
@@ -574,21 +589,28 @@ PrefillGroup tc_group(const wisp_layer *L, const void *x, const float *w, void *
     pg.out = reinterpret_cast<__nv_bfloat16 *>(out);
     pg.status = L->d_status;
     pg.wait_ns = L->wait_ns;
-    pg.ready = L->d_ready ? L->d_ready + (size_t)L->ready_parity * kBatchReadyWords : nullptr;
+    pg.trace = L->trace;
     return pg;
 }
 
-// The other counter half (zeroed by the launch about to use `ready`); flips
-// the parity for the next weight-stationary launch.
-uint32_t *take_ready_next(wisp_layer *L) {
-    if (!L->d_ready) return nullptr;
-    L->ready_parity ^= 1;
-    return L->d_ready + (size_t)L->ready_parity * kBatchReadyWords;
+// The counter halves of the next weight-stationary launch (it zeroes the
+// other halves for the launch after it); flips the parity.
+BatchCounters take_counters(wisp_layer *L) {
+    BatchCounters c{};
+    if (!L->d_ready || !L->d_combined) return c;
+    const size_t nd = (size_t)batch_done_words(L->H);
+    const int cur = L->ready_parity, nxt = cur ^ 1;
+    c.ready = L->d_ready + (size_t)cur * kBatchReadyWords;
+    c.ready_next = L->d_ready + (size_t)nxt * kBatchReadyWords;
+    c.done = L->d_combined + (size_t)cur * nd;
+    c.done_next = L->d_combined + (size_t)nxt * nd;
+    L->ready_parity = nxt;
+    return c;
 }
 
 int launch_tc_group(wisp_layer *L, Path path, const PrefillGroup &pg, cudaStream_t stream) {
     if (path == Path::kBatchTC) {
-        const int rc = launch_batch_group(pg, take_ready_next(L), stream);
+        const int rc = launch_batch_group(pg, take_counters(L), stream);
         if (!rc) L->launches += kBatchKernelsPerGroup;
         return rc;
     }
@@ -691,7 +713,7 @@ int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w,
         r.dev_status = L->d_dev_hdr + kHdrStatus;
         const int nu_bound = (int)std::min<long>(L->E, (long)T * K);
         const PrefillGroup pg = tc_group(L, x, w, out, 0, 0, T, K, nu_bound, nullptr);
-        int rc = launch_batch_resident(pg, r, take_ready_next(L), stream);
+        int rc = launch_batch_resident(pg, r, take_counters(L), stream);
         if (rc) return rc;
         L->launches += kBatchKernelsResident;
         WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
@@ -873,6 +895,11 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     // opts a paged layer in where the caller queues nothing on the device
     // while its forwards page in.
     L->async = (mode == WISP_MODE_RESIDENT);
+    {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 0;
+        L->tc_min_pairs = default_tc_min_pairs(hidden, inter, sms);
+    }
     const char *env = getenv("WISP_B200_SYNC");
     if (env && env[0] == '1') L->async = false;
     *out = L;
@@ -1115,6 +1142,27 @@ int wisp_layer_sync(wisp_layer *L) {
     int rc = drain(L);
     if (rc) return rc;
     return take_errors(L);
+}
+
+int wisp_layer_query(wisp_layer *L, int32_t key, int64_t *value) {
+    if (!L || !value) return fail(WISP_ERR_INVALID, "wisp_layer_query: NULL argument");
+    std::lock_guard<std::mutex> lk(L->mu);
+    switch (key) {
+        case WISP_CFG_ASYNC:
+            *value = L->async ? 1 : 0;
+            return WISP_OK;
+        case WISP_CFG_WAIT_NS:
+            *value = L->wait_ns;
+            return WISP_OK;
+        case WISP_CFG_TC_MIN_PAIRS:
+            *value = L->tc_min_pairs;
+            return WISP_OK;
+        case WISP_CFG_COMPUTE_CLASS:
+            *value = L->compute_class;
+            return WISP_OK;
+        default:
+            return fail(WISP_ERR_INVALID, "wisp_layer_query: unknown key");
+    }
 }
 
 int wisp_layer_config(wisp_layer *L, int32_t key, int64_t value) {

@@ -27,7 +27,7 @@ struct PrefillGroup {
     __nv_bfloat16 *out;             // [T][H]
     int *status;                    // sticky status word
     long long wait_ns;
-    uint32_t *ready;                // weight-stationary path: batch_ready_words(npairs, nu) words
+    unsigned long long *trace;      // debug milestones (weight-stationary kernel), or nullptr
 };
 
 // The tensor-core path covers hidden % 256 == 0 and inter % 128 == 0.
@@ -41,24 +41,31 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream);
 // expert, at most kBatchMaxPairs pairs per group).
 constexpr int kBatchTokens = 32;     // token rows per tile (the MMA's N)
 constexpr int kBatchMaxPairs = 256;  // pairs of one call (or group) on this path
-// Per-token-block counters + one abort word, per launch parity.
-constexpr long kBatchReadyWords = kBatchMaxPairs + (kBatchMaxPairs + kBatchTokens - 1) / kBatchTokens + 1;
+// Per-token-block counters, then a gathered-rows counter, the tile
+// scheduler's counter and an abort word.
+constexpr long kBatchReadyWords = kBatchMaxPairs + (kBatchMaxPairs + kBatchTokens - 1) / kBatchTokens + 3;
 
-// A group whose expert lists come from the pager (paged layers): gather,
-// one persistent gate-up + down launch, combine (3 kernels).  `p.ready` is
-// this launch's counter half, `ready_next` the other half (zeroed here for
-// the next launch).
-constexpr int kBatchKernelsPerGroup = 3;
-int launch_batch_group(const PrefillGroup &p, uint32_t *ready_next, cudaStream_t stream);
+// Per-launch counters of the path, two halves by launch parity: a launch
+// uses one half and zeroes the other for the next launch.
+__host__ __device__ inline int batch_done_words(int H) { return kBatchMaxPairs * (H / 256) * 4; }
+struct BatchCounters {
+    uint32_t *ready, *ready_next;  // kBatchReadyWords each: gate-up warps done per token block
+    uint32_t *done, *done_next;    // batch_done_words(H) each: down rows stored per token
+};
 
-// A whole call of a resident layer with no pager launch: the persistent
-// kernel routes the pairs itself (counting sort by expert in every CTA,
-// ascending pair order within an expert), gathers the hidden rows its tiles
-// read, counts the forward in the pager counters (forward, groups, unique
-// experts), then runs gate-up and down; the combine follows as a
-// programmatic dependent launch (2 kernels).  A routed id outside [0, E)
-// stops the call before any counter changes, records WISP_ERR_BAD_EXPERT in
-// the sticky word and in *dev_status (the combine then leaves out alone).
+// A group whose expert lists come from the pager (paged layers): gather and
+// one persistent launch that runs gate-up, down and the routing-order
+// combine of the group's tokens (2 kernels).
+constexpr int kBatchKernelsPerGroup = 2;
+int launch_batch_group(const PrefillGroup &p, const BatchCounters &c, cudaStream_t stream);
+
+// A whole call of a resident layer in one launch: the persistent kernel
+// routes the pairs itself (counting sort by expert in every CTA, ascending
+// pair order within an expert), gathers the hidden rows its tiles read,
+// counts the forward in the pager counters (forward, groups, unique experts),
+// then runs gate-up, down and the combine.  A routed id outside [0, E) stops
+// the call before any counter changes and records WISP_ERR_BAD_EXPERT in the
+// sticky word and in *dev_status; out is left alone.
 struct BatchRoute {
     const void *ids;
     int ids64, E, count_forward;
@@ -66,7 +73,7 @@ struct BatchRoute {
     int64_t *hdr;          // pager counters: [1] forward, [5] groups, [6] unique experts
     int32_t *dev_status;   // this call's routing status (device)
 };
-constexpr int kBatchKernelsResident = 2;
-int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, uint32_t *ready_next, cudaStream_t stream);
+constexpr int kBatchKernelsResident = 1;
+int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, const BatchCounters &c, cudaStream_t stream);
 
 }  // namespace wisp

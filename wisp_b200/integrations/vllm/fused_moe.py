@@ -133,7 +133,7 @@ class WispMoEState:
             "wisp_layer_create")
         self._h = handle
         self._b13, self._b2 = b13, b2
-        self.tc_min_pairs = _lib.TC_MIN_PAIRS_DEFAULT
+        self.tc_min_pairs = self._query(_lib.CFG_TC_MIN_PAIRS)
         self.last_unique_experts: set[int] = set()
         self.stats_pred_hits = 0
         self.stats_pred_total = 0
@@ -300,6 +300,11 @@ class WispMoEState:
         return {"groups": info[0], "misses": info[1], "pagein_bytes": info[2],
                 "unique_experts": info[3], "kernel_launches": n.value}
 
+    def _query(self, key: int) -> int:
+        v = ctypes.c_int64(0)
+        _lib.check(_lib.lib().wisp_layer_query(self._h, key, ctypes.byref(v)), "wisp_layer_query")
+        return int(v.value)
+
     def compute_class(self, pairs: int) -> str:
         """``"tc"`` when a call of ``pairs`` (token, k) pairs runs its expert
         compute on the tensor cores, else ``"cuda"`` (the library's rule)."""
@@ -329,7 +334,7 @@ class WispMoEState:
             if val is not None:
                 _lib.check(L.wisp_layer_config(self._h, key, int(val)), "configure")
         if tc_min_pairs is not None:
-            self.tc_min_pairs = int(tc_min_pairs)
+            self.tc_min_pairs = self._query(_lib.CFG_TC_MIN_PAIRS)
 
 
 # ---------------------------------------------------------------------------
