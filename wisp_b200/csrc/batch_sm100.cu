@@ -315,19 +315,31 @@ __device__ void route_pairs(const Args &g, Lists &L, unsigned char *scratch) {
     int *base = cnt + kMaxRouteExperts;           // [E] next list position of each expert
     int *emap = base + kMaxRouteExperts;          // [E] slot of each expert
     int *ids = emap + kMaxRouteExperts;           // [P]
+    // the ids (at most 2 per thread: P <= 256 < 2 * kThreads) and the map in flight together
+    constexpr int kIdsPerThread = (kMaxPairs + kThreads - 1) / kThreads;
+    long long v[kIdsPerThread];
+#pragma unroll
+    for (int j = 0; j < kIdsPerThread; ++j) {
+        const int p = tid + j * kThreads;
+        v[j] = p >= P ? 0
+                      : g.ids64 ? reinterpret_cast<const int64_t *>(g.ids)[p]
+                                : (long long)reinterpret_cast<const int32_t *>(g.ids)[p];
+    }
     for (int e = tid; e < E; e += blockDim.x) {
         cnt[e] = 0;
         emap[e] = g.emap[e];
     }
     __syncthreads();
     bool bad = false;
-    for (int p = tid; p < P; p += blockDim.x) {
-        const long long v = g.ids64 ? reinterpret_cast<const int64_t *>(g.ids)[p]
-                                    : (long long)reinterpret_cast<const int32_t *>(g.ids)[p];
-        const bool ok = v >= 0 && v < E;
-        bad |= !ok;
-        ids[p] = ok ? (int)v : 0;
-        if (ok) atomicAdd(&cnt[(int)v], 1);
+#pragma unroll
+    for (int j = 0; j < kIdsPerThread; ++j) {
+        const int p = tid + j * kThreads;
+        if (p < P) {
+            const bool ok = v[j] >= 0 && v[j] < E;
+            bad |= !ok;
+            ids[p] = ok ? (int)v[j] : 0;
+            if (ok) atomicAdd(&cnt[(int)v[j]], 1);
+        }
     }
     if (__syncthreads_or(bad)) {
         if (tid == 0) L.bad = 1;
