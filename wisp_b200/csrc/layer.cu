@@ -594,7 +594,8 @@ PrefillGroup tc_group(const wisp_layer *L, const void *x, const float *w, void *
 }
 
 // The counter halves of the next weight-stationary launch (it zeroes the
-// other halves for the launch after it); flips the parity.
+// other halves for the launch after it); flips the parity, which the caller
+// flips back when the launch is not queued (those halves were not zeroed).
 BatchCounters take_counters(wisp_layer *L) {
     BatchCounters c{};
     if (!L->d_ready || !L->d_combined) return c;
@@ -611,7 +612,10 @@ BatchCounters take_counters(wisp_layer *L) {
 int launch_tc_group(wisp_layer *L, Path path, const PrefillGroup &pg, cudaStream_t stream) {
     if (path == Path::kBatchTC) {
         const int rc = launch_batch_group(pg, take_counters(L), stream);
-        if (!rc) L->launches += kBatchKernelsPerGroup;
+        if (!rc)
+            L->launches += kBatchKernelsPerGroup;
+        else
+            L->ready_parity ^= 1;  // not queued: the next launch takes these halves again
         return rc;
     }
     const int rc = launch_prefill_group(pg, stream);
@@ -714,7 +718,10 @@ int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w,
         const int nu_bound = (int)std::min<long>(L->E, (long)T * K);
         const PrefillGroup pg = tc_group(L, x, w, out, 0, 0, T, K, nu_bound, nullptr);
         int rc = launch_batch_resident(pg, r, take_counters(L), stream);
-        if (rc) return rc;
+        if (rc) {
+            L->ready_parity ^= 1;  // not queued: the next launch takes these halves again
+            return rc;
+        }
         L->launches += kBatchKernelsResident;
         WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
         return WISP_OK;
