@@ -76,7 +76,8 @@ WISP_API int wisp_layer_destroy(wisp_layer *layer);
  *   x [T][H] bf16, topk_weights [T][k] fp32, topk_ids [T][k] int32 or int64
  *   (ids_int64 != 0), out [T][H] bf16.
  * Returns WISP_ERR_OVERFLOW when a single token routes to more unique
- * experts than the cap (the reference raises RuntimeError "...sub-batch...").
+ * experts than the cap (the reference raises RuntimeError "...sub-batch..."),
+ * WISP_ERR_INVALID for a resident layer before wisp_prime_identity.
  */
 WISP_API int wisp_moe_forward(wisp_layer *layer, const void *x, const float *topk_weights,
                      const void *topk_ids, int32_t ids_int64, int32_t num_tokens,
@@ -139,7 +140,8 @@ WISP_API int wisp_get_launch_count(wisp_layer *layer, int64_t *out);
  * (WISP_OK if none).  wisp_moe_forward returns before its work runs; a
  * device-side failure (a routed id outside [0, E), a bounded wait that ran
  * out) is reported by the next wisp_moe_forward or wisp_layer_sync.  After a
- * timeout the layer restarts cold (no slot resident; clock and counters kept).
+ * timeout a paged layer restarts cold (no slot resident; clock and counters
+ * kept); a resident layer keeps its slots.
  */
 WISP_API int wisp_layer_sync(wisp_layer *layer);
 

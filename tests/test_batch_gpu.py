@@ -161,3 +161,21 @@ def test_batch_bad_expert_reported_at_sync_then_recovers():
     out = fwd(st, x, w, ids)
     assert_parity(out, x, w13, w2, w, ids)
     st.close()
+
+
+def test_resident_forward_before_prime_is_rejected():
+    """A resident layer's slots are filled by prime_identity only: a forward
+    before it is an argument error on the host, not a read of empty slots."""
+    from wisp_b200.integrations.vllm.fused_moe import WispMoEState
+    E, H, I, T, K = 16, 256, 128, 16, 4
+    w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=41)
+    st = WispMoEState(w13, w2, E, "resident", DEV, 0)
+    for t in (1, T):   # the CUDA-core and the tensor-core class
+        with pytest.raises(_lib.WispError) as ei:
+            st.forward(x[:t].to(DEV), w[:t].to(DEV), ids[:t].to(DEV))
+        assert ei.value.code == _lib.WISP_ERR_INVALID
+    st.prime_identity()
+    st.configure(tc_min_pairs=1)
+    assert_parity(fwd(st, x, w, ids), x, w13, w2, w, ids)
+    st.close()
+

@@ -137,6 +137,7 @@ struct wisp_layer {
     int ready_parity = 0;            // the halves the next weight-stationary launch uses
     int tc_min_pairs = kPrefillMinPairs;  // calls of at least this many pairs run on the tensor cores
     int compute_class = 0;           // 0: by call size; 1: CUDA-core kernels; 2: tensor cores
+    bool primed = false;             // resident layer: every expert copied into its slot
     int32_t *h_mb = nullptr, *d_mb = nullptr;  // kMbRing mailboxes of mb_words words
     long mb_words = 0;
     int mb_next = 0;
@@ -478,9 +479,13 @@ int reset_cold(wisp_layer *L) {
     WISP_CUDA_TRY(cudaDeviceSynchronize());
     WISP_CUDA_TRY(cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords));
     WISP_CUDA_TRY(cudaMemset(L->d_flow, 0, sizeof(unsigned int) * kFlowWords));
-    WISP_CUDA_TRY(cudaMemset(L->d_s2e, 0xff, sizeof(int32_t) * L->cap));
-    WISP_CUDA_TRY(cudaMemset(L->d_emap, 0xff, sizeof(int32_t) * L->E));
-    WISP_CUDA_TRY(cudaMemset(L->d_tick, 0, sizeof(int64_t) * L->cap));
+    if (L->mode != WISP_MODE_RESIDENT) {
+        // a resident layer keeps its identity map: its slots still hold every
+        // expert (only wisp_prime_identity writes them)
+        WISP_CUDA_TRY(cudaMemset(L->d_s2e, 0xff, sizeof(int32_t) * L->cap));
+        WISP_CUDA_TRY(cudaMemset(L->d_emap, 0xff, sizeof(int32_t) * L->E));
+        WISP_CUDA_TRY(cudaMemset(L->d_tick, 0, sizeof(int64_t) * L->cap));
+    }
     WISP_CUDA_TRY(cudaMemcpy(L->d_slot_ready, L->d_slot_gen, sizeof(uint32_t) * L->cap,
                              cudaMemcpyDeviceToDevice));
     const int nblk = (std::max(L->H, 8) + 3) / 4;
@@ -949,6 +954,9 @@ int wisp_moe_forward(wisp_layer *L, const void *x, const float *topk_weights,
         return fail(WISP_ERR_INVALID, "wisp_moe_forward: x and out must be 16-byte aligned");
     std::lock_guard<std::mutex> lk(L->mu);
     DeviceGuard guard(L->dev);
+    if (L->mode == WISP_MODE_RESIDENT && !L->primed && num_tokens > 0)
+        return fail(WISP_ERR_INVALID,
+                    "wisp_moe_forward: resident layer has no expert in its slots; call wisp_prime_identity first");
     int rc = take_errors(L);
     if (rc) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -1024,6 +1032,7 @@ int wisp_prime_identity(wisp_layer *L, void *stream) {
                              cudaMemcpyDeviceToDevice));
     WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
     WISP_CUDA_TRY(cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(stream), L->ev_copies, 0));
+    L->primed = true;
     return WISP_OK;
 }
 
