@@ -159,13 +159,13 @@ WISP_API int wisp_layer_sync(wisp_layer *layer);
  * at most 32520 on 148 SMs) and the weight-stationary tensor-core kernel
  * (8 + 8 * grid words) fill with %globaltimer milestones; 0 = off), WISP_CFG_TC_MIN_PAIRS (calls of at least this many
  * (token, k) pairs run their expert compute on the tcgen05 tensor cores --
- * weight-stationary tiles up to 256 pairs, token-major GEMMs above -- where
+ * weight-stationary tiles up to 512 pairs, token-major GEMMs above -- where
  * hidden % 256 == 0 and inter % 128 == 0; smaller calls on the CUDA-core
  * decode kernels.  The choice depends on the call size only, so outputs stay
  * byte-identical across caps and modes; default: the smallest call whose
  * weight-stationary tiles, (I / 128 + H / 256) per pair at most, could fill
  * the GPU twice over -- 22 pairs at Qwen3-30B-A3B shapes on 148 SMs;
- * capped at 257),
+ * capped at 513),
  * WISP_CFG_COMPUTE_CLASS (0: by call size as above, the default; 1: the
  * CUDA-core kernels at any size; 2: the tensor cores at any size.  The two
  * tensor-core paths give identical bytes, the CUDA-core kernels differ in

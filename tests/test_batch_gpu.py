@@ -1,5 +1,5 @@
 """Decode batches on the weight-stationary tensor-core path (calls of
-tc_min_pairs <= T * k <= 256 pairs): parity with the fp32 CPU oracle under
+tc_min_pairs <= T * k <= 512 pairs): parity with the fp32 CPU oracle under
 the same bounds as the prefill path (mean-rel <= 1e-3; per element
 |out - ref| <= max(1e-2, 2 ulp(ref) + sum over k of 2 ulp(y_k)), the stored
 bf16 values may each round the other way with another fp32 accumulation
@@ -41,6 +41,8 @@ def assert_parity(out, x, w13, w2, w, ids):
     (128, 2048, 768, 16, 8, 128, "resident"),   # Qwen3-30B-A3B decode, batch 16
     (128, 2048, 768, 8, 8, 128, "resident"),    # batch 8 (64 pairs)
     (128, 2048, 768, 3, 8, 128, "resident"),    # batch 3 (24 pairs, above the default 22)
+    (128, 2048, 768, 64, 8, 128, "resident"),   # batch 64 (512 pairs: the largest call on this path)
+    (128, 2048, 768, 40, 8, 64, "paged"),       # 320 pairs, paged groups
     (128, 2048, 768, 16, 8, 40, "paged"),       # paged, several groups
     (8, 4096, 1536, 32, 2, 8, "resident"),      # Qwen3-235B hidden/inter, top-2, 8 tokens/expert
     (16, 256, 128, 64, 4, 16, "resident"),      # small shapes, > 32 pairs per expert (several token blocks)
@@ -70,15 +72,15 @@ def test_batch_byte_identical_across_caps_modes_and_placements():
 
 
 def test_batch_agrees_with_token_major_gemm():
-    """256 pairs run weight-stationary, 264 pairs token-major: the first 32
+    """512 pairs run weight-stationary, 520 pairs token-major: the first 64
     tokens' outputs (the same pairs) are byte-identical, so the two
     tensor-core paths are one numeric class."""
     E, H, I, K = 32, 512, 256, 8
-    w13, w2, x, w, ids = rand_case(E, H, I, 33, K, seed=23)
+    w13, w2, x, w, ids = rand_case(E, H, I, 65, K, seed=23)
     st = state(w13, w2, E, "resident")
-    big = fwd(st, x, w, ids)                    # 264 pairs: token-major GEMMs
-    small = fwd(st, x[:32], w[:32], ids[:32])   # 256 pairs: weight-stationary
-    assert torch.equal(big[:32], small)
+    big = fwd(st, x, w, ids)                    # 520 pairs: token-major GEMMs
+    small = fwd(st, x[:64], w[:64], ids[:64])   # 512 pairs: weight-stationary
+    assert torch.equal(big[:64], small)
     st.close()
 
 
@@ -91,7 +93,7 @@ def test_default_threshold_follows_the_expert_shape():
         w2 = torch.zeros(E, H, I, dtype=torch.bfloat16)
         st = state(w13, w2, E, "paged")
         per = I // 128 + H // 256
-        assert st.tc_min_pairs == min(max(-(-2 * sms // per), 1), 257), (E, H, I)
+        assert st.tc_min_pairs == min(max(-(-2 * sms // per), 1), 513), (E, H, I)
         st.close()
 
 

@@ -1,4 +1,4 @@
-"""Prefill-sized calls (T * k > 256) on the tcgen05 tensor-core path: parity
+"""Prefill-sized calls (T * k > 512) on the token-major tcgen05 GEMMs: parity
 with the fp32 CPU oracle with the reference's bf16 storage points (h, a, each
 weighted y and the output are stored bf16): mean-rel <= 1e-3 as in the decode
 tests, and per element |out - ref| <= max(1e-2, 2 ulp(out) + sum over k of
@@ -23,9 +23,9 @@ DEV = torch.device("cuda:0")
 
 
 @pytest.mark.parametrize("E,H,I,T,K,cap,mode", [
-    (16, 2048, 768, 64, 8, 16, "resident"),     # Qwen3-30B-A3B layer shapes, one group
-    (16, 2048, 768, 64, 8, 9, "paged"),         # several groups with page-in
-    (8, 4096, 1536, 160, 2, 8, "resident"),     # Qwen3-235B-A22B hidden/inter, top-2
+    (16, 2048, 768, 80, 8, 16, "resident"),     # Qwen3-30B-A3B layer shapes, one group
+    (16, 2048, 768, 80, 8, 9, "paged"),         # several groups with page-in
+    (8, 4096, 1536, 300, 2, 8, "resident"),     # Qwen3-235B-A22B hidden/inter, top-2
     (32, 256, 128, 300, 4, 32, "resident"),     # small shapes, many tokens per expert
 ])
 def test_prefill_matches_oracle(E, H, I, T, K, cap, mode):
@@ -47,7 +47,7 @@ def test_prefill_matches_oracle(E, H, I, T, K, cap, mode):
 
 
 def test_prefill_byte_identical_across_caps_and_modes():
-    E, H, I, T, K = 16, 512, 256, 48, 8
+    E, H, I, T, K = 16, 512, 256, 80, 8
     w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=7)
     outs = []
     for cap, mode in ((16, "resident"), (16, "paged"), (12, "paged"), (8, "paged")):
@@ -59,7 +59,7 @@ def test_prefill_byte_identical_across_caps_and_modes():
 
 
 def test_prefill_pager_state_and_kernel_count():
-    E, H, I, T, K, cap = 32, 256, 128, 80, 4, 10
+    E, H, I, T, K, cap = 32, 256, 128, 160, 4, 10
     w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=9)
     st = state(w13, w2, cap)
     oracle = PagerOracle(E, cap)

@@ -65,7 +65,7 @@ def test_mixtral_decode_paged(mixtral, cap):
 def test_mixtral_prefill_tensor_core_path(mixtral):
     w13, w2, g = mixtral
     st = state(w13, w2, 8, "resident")
-    T = 136  # 272 (token, k) pairs: beyond the decode range
+    T = 264  # 528 (token, k) pairs: beyond the weight-stationary range
     x = torch.randn(T, 4096, generator=g).to(torch.bfloat16)
     logits = torch.randn(T, 8, generator=g)
     w, ids = torch.softmax(logits, -1).topk(2, -1)

@@ -29,7 +29,7 @@ CFG_DROP_PAGEINS = 4
 CFG_TRACE_BUFFER = 5
 CFG_TC_MIN_PAIRS = 6
 CFG_COMPUTE_CLASS = 7
-PREFILL_MIN_PAIRS = 257     # calls from this size always run on the tensor cores
+PREFILL_MIN_PAIRS = 513     # calls from this size always run on the tensor cores (token-major GEMMs)
 
 _c_int32 = ctypes.c_int32
 _c_int64 = ctypes.c_int64

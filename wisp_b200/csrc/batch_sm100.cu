@@ -40,7 +40,7 @@
 // The expert lists come either from the pager (paged layers: u_off / u_pairs
 // / u_slot in global memory, X_perm written by the gather kernel) or, for a
 // resident layer's call, from the kernel itself: every CTA sorts the call's
-// (at most 256) pairs by expert in shared memory -- experts ascending, pairs
+// (at most 512) pairs by expert in shared memory -- experts ascending, pairs
 // ascending within an expert, slots from the expert map -- copies every
 // gridDim.x-th row of X_perm (its share) and counts itself in; a producer
 // waits for all CTAs' shares before its first gate-up load.
@@ -164,15 +164,18 @@ __device__ __forceinline__ int next_tile(Ring &R, int i, const Args &g, bool rel
 }
 
 // The call's (or group's) experts, their token blocks and pair lists.
+// Index arrays are 16-bit (offsets <= 512, blocks <= 528, slots < 1024) so
+// that 512 pairs' lists fit beside the 6-stage ring.
 struct Lists {
     int nu, nblocks, bad;
-    int off[kMaxPairs + 1];    // pair-list offsets
-    int first[kMaxPairs + 1];  // first token block of each expert (prefix of block counts)
-    int pairs[kMaxPairs];      // routed lists: absolute pair index, expert-major
-    int slot[kMaxPairs];       // routed lists: slot of each expert
-    int rows[kMaxBlocks];      // rows of each token block
-    int order[kMaxBlocks];     // blocks by rows, most first (ties: lower block first)
+    int pairs[kMaxPairs];          // routed lists: absolute pair index, expert-major
+    int16_t off[kMaxPairs + 1];    // pair-list offsets
+    int16_t first[kMaxPairs + 1];  // first token block of each expert (prefix of block counts)
+    int16_t slot[kMaxPairs];       // slot of each expert
+    int16_t rows[kMaxBlocks];      // rows of each token block
+    int16_t order[kMaxBlocks];     // blocks by rows, most first (ties: lower block first)
 };
+static_assert(kMaxPairs + 1 <= 32767 && kMaxBlocks <= 32767 && kMaxRouteExperts <= 32767, "16-bit lists");
 
 // Token block b -> expert u, first list position q0, rows.
 __device__ __forceinline__ void block_of(const Lists &L, int b, int &u, int &q0, int &rows) {
@@ -315,7 +318,7 @@ __device__ void route_pairs(const Args &g, Lists &L, unsigned char *scratch) {
     int *base = cnt + kMaxRouteExperts;           // [E] next list position of each expert
     int *emap = base + kMaxRouteExperts;          // [E] slot of each expert
     int *ids = emap + kMaxRouteExperts;           // [P]
-    // the ids (at most 2 per thread: P <= 256 < 2 * kThreads) and the map in flight together
+    // the ids (at most 3 per thread: P <= 512 <= 3 * kThreads) and the map in flight together
     constexpr int kIdsPerThread = (kMaxPairs + kThreads - 1) / kThreads;
     long long v[kIdsPerThread];
 #pragma unroll
@@ -367,8 +370,8 @@ __device__ void route_pairs(const Args &g, Lists &L, unsigned char *scratch) {
         for (int e = e0; e < e1; ++e) {
             const int c = cnt[e];
             if (c > 0) {
-                L.off[u] = at;
-                L.slot[u] = emap[e];
+                L.off[u] = (int16_t)at;
+                L.slot[u] = (int16_t)emap[e];
                 base[e] = at;
                 ++u;
                 at += c;
@@ -376,7 +379,7 @@ __device__ void route_pairs(const Args &g, Lists &L, unsigned char *scratch) {
         }
         if (lane == 31) {
             L.nu = iu;
-            L.off[iu] = P;
+            L.off[iu] = (int16_t)P;
         }
         __syncwarp();
         // placement, 32 pairs at a time in ascending order
@@ -430,8 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         pairs = L.pairs;
     } else {
         const int nu = min(gemm::group_experts(g.nu_dev, g.pager_status), kMaxPairs);
-        for (int i = threadIdx.x; i <= nu; i += blockDim.x) L.off[i] = g.u_off[i];
-        for (int i = threadIdx.x; i < nu; i += blockDim.x) L.slot[i] = g.u_slot[i];
+        for (int i = threadIdx.x; i <= nu; i += blockDim.x) L.off[i] = (int16_t)g.u_off[i];
+        for (int i = threadIdx.x; i < nu; i += blockDim.x) L.slot[i] = (int16_t)g.u_slot[i];
         if (threadIdx.x == 0) L.nu = nu;
         pairs = g.u_pairs;
         __syncthreads();
@@ -449,11 +452,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         int acc = inc - nb;
         for (int e = e0; e < e1; ++e) {
-            L.first[e] = acc;
+            L.first[e] = (int16_t)acc;
             acc += (L.off[e + 1] - L.off[e] + kTN - 1) / kTN;
         }
         if (lane == 31) {
-            L.first[nu] = inc;
+            L.first[nu] = (int16_t)inc;
             L.nblocks = inc;
         }
     }
@@ -461,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = threadIdx.x; b < L.nblocks; b += blockDim.x) {
         int u, q0, rows;
         block_of(L, b, u, q0, rows);
-        L.rows[b] = rows;
+        L.rows[b] = (int16_t)rows;
     }
     __syncthreads();
     for (int b = threadIdx.x; b < L.nblocks; b += blockDim.x) {
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rc = L.rows[c];
             rank += (rc > rb) || (rc == rb && c < b);
         }
-        L.order[rank] = b;
+        L.order[rank] = (int16_t)b;
     }
     if (threadIdx.x == 0) {
         R.abort = 0;
@@ -753,7 +756,7 @@ int check_group(const PrefillGroup &p, const BatchCounters &c) {
     if (!prefill_shapes_supported(p.H, p.I))
         return set_error("wisp: tensor-core path needs hidden % 256 == 0 and inter % 128 == 0"), WISP_ERR_UNSUPPORTED;
     if (p.npairs > kMaxPairs)
-        return set_error("wisp: weight-stationary path takes at most 256 pairs per call"), WISP_ERR_INVALID;
+        return set_error("wisp: weight-stationary path takes at most 512 pairs per call"), WISP_ERR_INVALID;
     if (!c.ready || !c.ready_next || !c.done || !c.done_next)
         return set_error("wisp: batch path without its counters"), WISP_ERR_INVALID;
     return WISP_OK;

@@ -91,7 +91,7 @@ constexpr long long kDefaultWaitNs = 10LL * 1000 * 1000 * 1000;
 // Calls of T * k pairs in [tc_min_pairs, kPrefillMinPairs) run on the
 // weight-stationary tensor-core path, larger ones on the token-major GEMMs,
 // smaller ones on the CUDA-core decode kernels.
-constexpr int kPrefillMinPairs = 257;
+constexpr int kPrefillMinPairs = kBatchMaxPairs + 1;
 
 // Default tensor-core threshold of a layer: the smallest call whose
 // weight-stationary tiles -- I / 128 gate-up + H / 256 down per pair at most
@@ -694,7 +694,7 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
 }
 
 // Resident layers run the tensor-core paths without a host round trip.  Up
-// to 256 pairs the weight-stationary kernel routes the call itself (no pager
+// to 512 pairs the weight-stationary kernel routes the call itself (no pager
 // launch: a resident layer's pager step only counts the forward, which that
 // kernel does).  Larger calls: the pager (one group, slots fixed) leaves the
 // expert lists and count on the device and the GEMM kernels read them there.

@@ -40,7 +40,7 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream);
 // Weight-stationary tensor-core path for decode batches (few tokens per
 // expert, at most kBatchMaxPairs pairs per group).
 constexpr int kBatchTokens = 32;     // token rows per tile (the MMA's N)
-constexpr int kBatchMaxPairs = 256;  // pairs of one call (or group) on this path
+constexpr int kBatchMaxPairs = 512;  // pairs of one call (or group) on this path
 // Per-token-block counters, then a gathered-rows counter, the tile
 // scheduler's counter and an abort word.
 constexpr long kBatchReadyWords = kBatchMaxPairs + (kBatchMaxPairs + kBatchTokens - 1) / kBatchTokens + 3;
