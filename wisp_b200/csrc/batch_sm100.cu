@@ -12,7 +12,7 @@
 //            (M 128, N 32, K 16) per K step on the same token tile; thread
 //            (TMEM lane) r holds g and u of intermediate row j + r for the
 //            block's tokens and stores act_perm[q][j + r] =
-//            bf16(silu(bf16(g)) * bf16(u));
+//            bf16(bf16(silu(bf16(g))) * bf16(u));
 //   down     tile (token block b, 256 hidden rows h):
 //            Y0 / Y1 [128 x 32] = W2 rows h / h + 128 . act_perm rows^T over
 //            K = I; y[pair][h + r] = bf16(acc * routing weight).
@@ -265,8 +265,8 @@ __device__ __forceinline__ unsigned char *align1024(unsigned char *p) {
 // n, all rows at once, acquire-release at GPU scope after a warp barrier, so
 // the other lanes' stores are released too); the warp that brings a (token,
 // 256-row block, quarter) counter to top-k holds the last of the token's
-// weighted rows there and writes out[t] = the routing-order fp32 sum of the
-// bf16 rows y[t * K + k], rounded to bf16 (the combine kernel's
+// weighted rows there and writes out[t] = the routing-order sum of the bf16
+// rows y[t * K + k] (combine_add), rounded to bf16 (the combine kernel's
 // arithmetic), loading up to 8 rows at a time past L1 before summing them.
 __device__ __forceinline__ void combine_rows(const Args &g, const int32_t *pairs, int q0, int rows, int col,
                                              int quarter, int lane, int h) {
@@ -298,8 +298,8 @@ __device__ __forceinline__ void combine_rows(const Args &g, const int32_t *pairs
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 if (k0 + j < K) {
-                    a0 += bf16lo((uint32_t)v0[j]);
-                    a1 += bf16lo((uint32_t)v1[j]);
+                    a0 = combine_add(a0, bf16lo((uint32_t)v0[j]), K);
+                    a1 = combine_add(a1, bf16lo((uint32_t)v1[j]), K);
                 }
             }
         }
@@ -677,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (n < rows) {
                         const float gv = round_bf16(__uint_as_float(d0[n]));
                         const float uv = round_bf16(__uint_as_float(d1[n]));
-                        dst[(size_t)n * I] = act_value(gv / (1.0f + expf(-gv)) * uv);
+                        dst[(size_t)n * I] = act_value(silu_stored(gv) * uv);
                     }
                 }
                 fence_proxy_async_global();

@@ -59,6 +59,16 @@ __device__ __forceinline__ float dot8(const uint4 &w, const uint4 &x, float acc)
 // element the one-launch forward has not written yet, so a result with that
 // pattern is stored as the canonical NaN instead (every path does the same).
 constexpr unsigned short kActEmpty = 0xFFFFu;
+// The reference's storage points around the activation and the combine
+// (vLLM's silu_and_mul and moe_sum, pinned by golden outputs of vLLM's
+// fused_experts): silu(g) is stored bf16 before it multiplies u, and the k
+// weighted rows of a token are added in bf16 -- every partial sum rounded --
+// for top-k <= 4, in fp32 above.
+__device__ __forceinline__ float silu_stored(float g) { return round_bf16(g / (1.0f + expf(-g))); }
+__device__ __forceinline__ float combine_add(float acc, float v, int K) {
+    return K <= 4 ? round_bf16(acc + v) : acc + v;
+}
+
 __device__ __forceinline__ __nv_bfloat16 act_value(float v) {
     __nv_bfloat16 b = __float2bfloat16_rn(v);
     if (__bfloat16_as_ushort(b) == kActEmpty) b = __ushort_as_bfloat16((unsigned short)0x7FFFu);

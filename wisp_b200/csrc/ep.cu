@@ -11,7 +11,8 @@
 //                     weight) record;
 //   ep_pack_kernel    one warp per pair: x[t] -> send row pos[p];
 //   ep_combine_kernel out[t] = sum over k in routing order of the returned
-//                     weighted rows, fp32, stored bf16 -- the same sum as the
+//                     weighted rows (combine_add: bf16 partial sums for
+//                     top-k <= 4, fp32 above), stored bf16 -- the same sum as the
 //                     one-GPU forward, so the result is byte-identical to it.
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -100,8 +101,8 @@ __global__ void ep_combine_kernel(const uint4 *y, const int32_t *pos, int T, int
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            acc[2 * j] += bf16lo(wv[j]);
-            acc[2 * j + 1] += bf16hi(wv[j]);
+            acc[2 * j] = combine_add(acc[2 * j], bf16lo(wv[j]), K);
+            acc[2 * j + 1] = combine_add(acc[2 * j + 1], bf16hi(wv[j]), K);
         }
     }
     uint32_t o[4];

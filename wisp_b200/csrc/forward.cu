@@ -355,7 +355,7 @@ __device__ __forceinline__ void gu_pass(const GroupCompute &a, const Meta &m, in
         const float g = round_bf16(warp_sum(ag[t]));
         const float v = round_bf16(warp_sum(au[t]));
         if (lane == kPubLane) {  // one lane stores every pair's row j
-            const float sg = g / (1.0f + expf(-g));
+            const float sg = silu_stored(g);
             st_relaxed_bf16(a.act + (size_t)m.pair[qb + t] * I + j, act_value(sg * v));
         }
     }

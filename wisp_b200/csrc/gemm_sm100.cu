@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int h = 0; h < 2; ++h) {
                             const float gv = round_bf16(__uint_as_float(gr[k + h]));
                             const float uv = round_bf16(__uint_as_float(ur[k + h]));
-                            o[h] = gv / (1.0f + expf(-gv)) * uv;
+                            o[h] = silu_stored(gv) * uv;
                         }
                         packed[k / 2] = (uint32_t)__bfloat16_as_ushort(act_value(o[0])) |
                                         ((uint32_t)__bfloat16_as_ushort(act_value(o[1])) << 16);
@@ -259,8 +259,8 @@ __global__ void combine_kernel(const uint4 *y, int t0, int t1, int K, int H8, ui
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            acc[2 * j] += bf16lo(wv[j]);
-            acc[2 * j + 1] += bf16hi(wv[j]);
+            acc[2 * j] = combine_add(acc[2 * j], bf16lo(wv[j]), K);
+            acc[2 * j + 1] = combine_add(acc[2 * j + 1], bf16hi(wv[j]), K);
         }
     }
     uint32_t o[4];

@@ -10,11 +10,11 @@
 //               intermediate: D[128 x 256] = X_perm rows . [W13 gate rows j ;
 //               up rows I + j]^T over K = H, so each thread of the epilogue
 //               holds g and u of the same (pair, j) and stores
-//               act_perm[q][j] = bf16(silu(bf16(g)) * bf16(u));
+//               act_perm[q][j] = bf16(bf16(silu(bf16(g))) * bf16(u));
 //   down        per expert u and tile of 128 pairs x 256 hidden rows h:
 //               D = act_perm rows . W2 rows^T over K = I; the epilogue stores
 //               y[pair][h] = bf16(D * routing weight);
-//   combine     out[t] = sum over k in routing order of y[t*K + k] (fp32, bf16).
+//   combine     out[t] = sum over k in routing order of y[t*K + k] (combine_add, bf16).
 //
 // Kernel structure (persistent: at most one CTA of 6 warps per SM, each
 // looping over output tiles in N-fastest order, so consecutive tiles share the

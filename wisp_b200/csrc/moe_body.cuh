@@ -3,9 +3,10 @@
 // run exactly the same arithmetic:
 //   h = W13[s] . x[t]   fp32 FMA chain per lane over 16-byte chunks lane, lane+32, ...,
 //                       fixed butterfly, stored bf16 (gate rows 0..I-1, up rows I..2I-1)
-//   a = silu(g) * u     fp32 from the stored values, stored bf16
+//   a = silu(g) * u     from the stored values, silu(g) stored bf16 first, a stored bf16
 //   y = (W2[s] . a) * w fp32, weight applied in fp32, stored bf16
-//   out[t] = sum_k y    k in routing order, fp32, stored bf16
+//   out[t] = sum_k y    k in routing order: bf16 partial sums for top-k <= 4,
+//                       fp32 above; stored bf16 (common.cuh: combine_add)
 // (vLLM fused_experts' storage points, as called by the reference at
 // src/wisp/integrations/vllm/fused_moe.py:1106-1118 and :1155-1167.)
 #pragma once
@@ -81,7 +82,7 @@ __device__ __forceinline__ void gateup_rowpair(const GroupCompute &a, int u, int
                 const float g = round_bf16(warp_sum(ag[i]));
                 const float v = round_bf16(warp_sum(au[i]));
                 if (lane == i) {
-                    const float s = g / (1.0f + expf(-g));
+                    const float s = silu_stored(g);
                     const int p = a.u_pairs[qb + i];
                     a.act[(size_t)p * I + j] = act_value(s * v);
                 }
@@ -199,7 +200,7 @@ __device__ __forceinline__ void combine_rows(const GroupCompute &a, int h0, int 
         if (hh >= H) continue;
         float acc = 0.f;
         for (int k = 0; k < K; ++k)
-            acc += __bfloat162float(__ldcg(a.y + ((size_t)t * K + k) * H + hh));
+            acc = combine_add(acc, __bfloat162float(__ldcg(a.y + ((size_t)t * K + k) * H + hh)), K);
         a.out[(size_t)t * H + hh] = __float2bfloat16_rn(acc);
     }
 }
