@@ -3,9 +3,11 @@ collective sequence (counts, rows, records, results) with the CUDA route /
 pack / combine kernels and the expert compute replaced by torch stand-ins.
 
 Checks the combine against a direct computation, the order in which each
-owner receives its rows ((source rank, pair) order, local ids), and that an
+owner receives its rows ((source rank, pair) order, local ids), that an
 expert id out of range on one rank raises on every rank with no collective
-left waiting."""
+left waiting, and that sources of different call sizes have their rows
+computed in their own classes (one local call per run of same-class
+sources, each forced to its class, the size rule restored after)."""
 import os
 import socket
 
@@ -127,3 +129,50 @@ def _free_port():
 @pytest.mark.parametrize("world", [2, 4])
 def test_ep_collectives_gloo(world):
     mp.start_processes(_worker, args=(world, _free_port()), nprocs=world, start_method="spawn")
+
+
+def _mixed_worker(rank, world, port):
+    """Rank r routes T_r tokens: the fake layer's class rule (>= 10 pairs:
+    "tc") puts ranks 0 and 1 on one side and ranks 2 and 3 on the other, so
+    an owner receives runs of sources [tc, tc, cuda, cuda]."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        per = E // world
+        Ts = [5, 4, 3, 2][:world]   # x K = 3: 15, 12 pairs ("tc"); 9, 6 ("cuda")
+        local = _FakeExperts(rank, per)
+        layer = _CpuEP(None, None, E, per, local=local, device="cpu")
+        g = torch.Generator().manual_seed(7 + rank)
+        T = Ts[rank]
+        ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).to(torch.int32)
+        w = torch.rand((T, K), generator=g)
+        x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+        out = layer.forward(x, w, ids)
+        acc = torch.zeros((T, H))
+        for k in range(K):
+            acc += (x.float() * (ids[:, k].long() + 1).view(-1, 1).float() * w[:, k:k + 1]).to(torch.bfloat16).float()
+        assert torch.equal(out, acc.to(torch.bfloat16)), f"rank {rank}: combine differs"
+        # what this owner received from each source, and the calls it made
+        counts = torch.zeros(world, dtype=torch.int64)
+        for src in range(world):
+            gs = torch.Generator().manual_seed(7 + src)
+            sids = torch.stack([torch.randperm(E, generator=gs)[:K] for _ in range(Ts[src])])
+            counts[src] = int(((sids.reshape(-1) // per) == rank).sum())
+        expect_runs = []
+        for src in range(world):
+            cls = "tc" if Ts[src] * K >= 10 else "cuda"
+            if counts[src]:
+                if expect_runs and expect_runs[-1][0] == cls:
+                    expect_runs[-1][1] += int(counts[src])
+                else:
+                    expect_runs.append([cls, int(counts[src])])
+        assert local.classes == [c for c, _ in expect_runs] + ["auto"], (rank, local.classes, expect_runs)
+        assert [len(v) for v in local.seen] == [n for _, n in expect_runs], (rank, expect_runs)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_mixed_call_sizes_gloo():
+    mp.start_processes(_mixed_worker, args=(4, _free_port()), nprocs=4, start_method="spawn")
