@@ -68,48 +68,88 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons of the given GPUs, sampled every 0.2 s
+    during the timed region by in-process NVML queries (read-only; no
+    subprocess is started while the GPUs run).  Falls back to nvidia-smi when
+    NVML cannot be loaded.  Under torchrun only rank 0 samples (every rank's
+    GPU), so N processes do not contend for the host during the timed region."""
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
-        self.rows = []
+    def __init__(self, indices, enabled: bool = True):
+        self.indices = [int(i) for i in (indices if isinstance(indices, (list, tuple)) else [indices])]
+        self.enabled = enabled
+        self.rows = []          # (sm_mhz, sm_max_mhz, [reason names])
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        self._handles = []
+
+    def _open_nvml(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.indices]
+            self._nvml = pynvml
+        except Exception:
+            self._nvml = None
+
+    def _sample_nvml(self):
+        nv = self._nvml
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        for h in self._handles:
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.rows.append((float(sm), float(mx), [n for n, b in zip(self.NAMES, bits) if r & b]))
+
+    def _sample_smi(self):
+        for i in self.indices:
+            out = subprocess.run(["nvidia-smi", "-i", str(i), f"--query-gpu={self.Q}",
+                                  "--format=csv,noheader,nounits"], capture_output=True,
+                                 text=True, timeout=5).stdout.strip()
+            if not out:
+                continue
+            c = [x.strip() for x in out.split(",")]
+            num = [float(v) if v.replace(".", "").isdigit() else None for v in c[1:3]]
+            reasons = [n for k, n in enumerate(self.NAMES) if len(c) > 5 + k
+                       and c[5 + k].lower().startswith("active")]
+            if num[0] is not None and num[1] is not None:
+                self.rows.append((num[0], num[1], reasons))
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True,
-                                     text=True, timeout=5).stdout.strip()
-                if out:
-                    self.rows.append([c.strip() for c in out.split(",")])
+                self._sample_nvml() if self._nvml is not None else self._sample_smi()
             except Exception:
                 pass
             self._stop.wait(0.2)
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._run, daemon=True)
-        self._t.start()
+        if self.enabled:
+            self._open_nvml()
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        self._t.join(timeout=10)
+        if self._t is not None:
+            self._stop.set()
+            self._t.join(timeout=10)
 
     def summary(self):
+        if not self.enabled:
+            return None
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if len(r) > 5 + i and r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows),
+                "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": sorted({n for r in self.rows for n in r[2]}),
+                "samples": len(self.rows), "gpus": self.indices,
+                "via": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
 def h2d_peak_gbs(dev, nbytes=1 << 30, reps=6):
@@ -518,7 +558,7 @@ def run_wisp_ep(args):
     tel0 = [lay.local.telemetry() for lay in layers]
     dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clk = ClockSampler(dev.index)
+    clk = ClockSampler(list(range(world)), enabled=rank == 0)
     with clk:
         torch.cuda.synchronize()
         ev0.record()

@@ -128,6 +128,17 @@ WISP_API int wisp_layer_buffers(wisp_layer *layer, void **scratch_w13, void **sc
 WISP_API int wisp_get_telemetry(wisp_layer *layer, int64_t *out4);
 
 /*
+ * The unique expert ids, ascending, of this layer's last paged forward
+ * (synchronises the device): the reference's WispMoEState.last_unique_experts
+ * (fused_moe.py:1170-1176), which snapshot_expert_stats reports as the working
+ * set (:579-593) and prefetch_async keeps out of its victims (:360-433).  A
+ * resident forward leaves it unchanged, as the reference's does.  Writes at
+ * most max_ids ids; *n_out = the number of unique experts.
+ */
+WISP_API int wisp_get_last_unique_experts(wisp_layer *layer, int32_t *ids_out, int32_t max_ids,
+                                          int32_t *n_out);
+
+/*
  * Number of CUDA kernels this layer has launched so far, on every path (one
  * per asynchronous forward; pager plus two per token group on the synchronous
  * path).  No counterpart in the reference; used to account for launches.
@@ -199,9 +210,15 @@ WISP_API int wisp_layer_query(wisp_layer *layer, int32_t key, int64_t *value);
  * [T][k] fp32, out [T][H] bf16.  Intermediates live in one static device
  * array of about 6.3 MB per GPU, held until exit: T*k <= 128, hidden <= 8192,
  * inter <= 16384; larger sizes return WISP_ERR_INVALID.  Calls share that
- * array, so calls that overlap on the GPU race.  The first call on a device
- * resolves the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture.
+ * array, so calls that overlap on the GPU race.  CUDA loads device code, and
+ * with it this array, onto a GPU lazily: the array takes its device memory at
+ * the first call on that device, not when the library is loaded.  A call with
+ * num_tokens == 0 (the other arguments except device are then ignored) does
+ * only that set-up -- places the array and the kernels' code on `device` and
+ * resolves the array's address (cudaGetSymbolAddress) with that device
+ * current -- and computes nothing; make it at start-up, before reserving the
+ * free HBM and before any stream capture.  From then on the GPU holds the
+ * array until the process exits.
  */
 WISP_API int wisp_expert_compute_noalloc(int32_t device, const void *x, const void *scratch_w13,
                                          const void *scratch_w2, int32_t num_slots,

@@ -77,6 +77,39 @@ def test_noalloc_matches_forward_on_two_calls_paged():
     st.close()
 
 
+def test_noalloc_takes_no_device_memory_after_setup():
+    """A zero-token call places the static array and the kernels' code on the
+    device; after it (and a first compute call), a call leaves the device's
+    free memory and torch's allocator untouched.  The largest call the array
+    admits, 128 pairs at top_k 1, matches the regular forward."""
+    from wisp_b200.integrations.vllm.fused_moe import WispMoEState
+    E, H, I, K, T = 64, 1024, 512, 1, 128
+    w13, w2, g = _case(E, H, I, T, K, seed=23)
+    st = WispMoEState(w13, w2, E, "resident", DEV, 0)
+    st.prime_identity()
+    L = _lib.lib()
+    _lib.check(L.wisp_expert_compute_noalloc(DEV.index, None, None, None, 0, None, None, 0, 0, 0, 0,
+                                             None, None), "set-up call")
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    w, ids = wl.softmax_topk(torch.randn(T, E, generator=g), K)
+    w, ids = w.to(DEV), ids.to(DEV)
+    slots = ids.to(torch.int32).contiguous()
+    ref = st.forward(x, w, ids)
+    out = torch.full_like(x, float("nan"))
+    _noalloc(st, x, w, slots, out)                 # first compute call
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(DEV)
+    alloc0 = torch.cuda.memory_allocated(DEV)
+    out.fill_(float("nan"))
+    _noalloc(st, x, w, slots, out)                 # second call: nothing may be allocated
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(DEV)
+    assert (free1, torch.cuda.memory_allocated(DEV)) == (free0, alloc0)
+    c = compare(out.cpu(), ref.cpu().float())
+    assert c["max_abs"] <= 1e-2 and c["mean_rel"] <= 1e-3, c
+    st.close()
+
+
 def test_noalloc_rejects_sizes_beyond_the_static_scratch():
     L = _lib.lib()
     rc = L.wisp_expert_compute_noalloc(0, None, None, None, 8, None, None, 17, 8, 2048, 768, None,

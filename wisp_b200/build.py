@@ -15,6 +15,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -54,15 +55,21 @@ def build(force: bool = False, verbose: bool = False) -> str:
     objdir = os.path.join(LIBDIR, "_obj")
     os.makedirs(objdir, exist_ok=True)
     nvcc = _nvcc()
-    objs = []
+    cmds, objs = [], []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src).replace(".cu", ".o"))
-        cmd = [nvcc, *ARCH, *FLAGS, "-I", INCLUDE, "-dc" if False else "-c", src, "-o", obj]
+        cmd = [nvcc, *ARCH, *FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(obj)
+    # one nvcc per translation unit, in parallel
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as pool:
+        for r in pool.map(lambda c: subprocess.run(c, capture_output=not verbose, text=True), cmds):
+            if r.returncode:
+                sys.stderr.write((r.stdout or "") + (r.stderr or ""))
+                raise subprocess.CalledProcessError(r.returncode, r.args)
     tmp = LIB + ".tmp"
     subprocess.run([nvcc, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs], check=True)
     os.replace(tmp, LIB)

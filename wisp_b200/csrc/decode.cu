@@ -60,7 +60,22 @@ int launch_variant(const GroupCompute &g, int max_nu, cudaStream_t stream) {
     return WISP_OK;
 }
 
+template <int MAXP>
+cudaError_t preload_variant() {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, gateup_silu_kernel<MAXP>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, down_combine_kernel<MAXP>);
+    return e;
+}
+
 }  // namespace
+
+int preload_decode_kernels() {
+    for (cudaError_t e : {preload_variant<1>(), preload_variant<2>(), preload_variant<4>(),
+                          preload_variant<8>(), preload_variant<16>()})
+        WISP_CUDA_TRY(e);
+    return WISP_OK;
+}
 
 int launch_decode_group(const GroupCompute &g, int max_nu, cudaStream_t stream) {
     if (max_nu <= 0 || g.t1 <= g.t0) return WISP_OK;

@@ -29,4 +29,9 @@ struct GroupCompute {
 constexpr int kDecodeKernelsPerGroup = 2;
 int launch_decode_group(const GroupCompute &g, int max_nu, cudaStream_t stream);
 
+// Load the decode kernels' code onto the current device now (CUDA loads
+// device code lazily, at a kernel's first launch, and loading takes device
+// memory); for callers that must not take device memory later.
+int preload_decode_kernels();
+
 }  // namespace wisp

@@ -120,6 +120,7 @@ struct wisp_layer {
     int32_t *d_s2e = nullptr, *d_emap = nullptr;
     int64_t *d_tick = nullptr, *d_hdr = nullptr;
     uint32_t *d_slot_gen = nullptr, *d_slot_ready = nullptr;
+    uint32_t *d_last_unique = nullptr;  // bitmap of the last paged forward's unique experts
     unsigned int *d_bar = nullptr;
     unsigned int *d_flow = nullptr;  // forward-kernel dataflow words (kFlowWords)
     int kparity = 0;                 // parity of the forward-kernel launches
@@ -452,6 +453,7 @@ void fill_pager_params(wisp_layer *L, PagerParams &p, const void *ids, int ids64
     p.emap = L->d_emap;
     p.hdr = L->d_hdr;
     p.slot_gen = L->d_slot_gen;
+    p.last_unique = L->d_last_unique;
     p.slots = L->d_slots;
     p.grp_start = L->d_grp_start;
     p.grp_nu = L->d_grp_nu;
@@ -876,11 +878,13 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     if (cudaMalloc(&L->d_emap, sizeof(int32_t) * num_experts) != cudaSuccess ||
         cudaMalloc(&L->d_hdr, sizeof(int64_t) * 8) != cudaSuccess ||
         cudaMalloc(&L->d_bar, sizeof(unsigned int) * kBarWords) != cudaSuccess ||
+        cudaMalloc(&L->d_last_unique, sizeof(uint32_t) * 32) != cudaSuccess ||
         cudaMalloc(&L->d_flow, sizeof(unsigned int) * kFlowWords) != cudaSuccess)
         return bail(fail(WISP_ERR_NOMEM, "wisp_layer_create: device allocation failed"));
     if (cudaMemset(L->d_emap, 0xff, sizeof(int32_t) * num_experts) != cudaSuccess ||
         cudaMemset(L->d_hdr, 0, sizeof(int64_t) * 8) != cudaSuccess ||
         cudaMemset(L->d_bar, 0, sizeof(unsigned int) * kBarWords) != cudaSuccess ||
+        cudaMemset(L->d_last_unique, 0, sizeof(uint32_t) * 32) != cudaSuccess ||
         cudaMemset(L->d_flow, 0, sizeof(unsigned int) * kFlowWords) != cudaSuccess ||
         cudaHostAlloc(&L->h_done, sizeof(unsigned long long), cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer((void **)&L->d_done, L->h_done, 0) != cudaSuccess ||
@@ -926,7 +930,7 @@ int wisp_layer_destroy(wisp_layer *L) {
     free_ws(L);
     for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->d_s2e, (void *)L->d_tick, (void *)L->d_emap,
                     (void *)L->d_hdr, (void *)L->d_slot_gen, (void *)L->d_slot_ready, (void *)L->d_bar,
-                    (void *)L->d_flow})
+                    (void *)L->d_flow, (void *)L->d_last_unique})
         cudaFree(p);
     if (L->h_done) cudaFreeHost(L->h_done);
     if (L->h_status) cudaFreeHost(L->h_status);
@@ -1141,6 +1145,24 @@ int wisp_get_telemetry(wisp_layer *L, int64_t *out4) {
     out4[1] = hdr[2];
     out4[2] = hdr[2] * (L->b13 + L->b2);
     out4[3] = hdr[6];
+    return WISP_OK;
+}
+
+int wisp_get_last_unique_experts(wisp_layer *L, int32_t *ids_out, int32_t max_ids, int32_t *n_out) {
+    if (!L || !n_out || max_ids < 0 || (max_ids > 0 && !ids_out))
+        return fail(WISP_ERR_INVALID, "wisp_get_last_unique_experts: bad argument");
+    std::lock_guard<std::mutex> lk(L->mu);
+    DeviceGuard guard(L->dev);
+    WISP_CUDA_TRY(cudaDeviceSynchronize());
+    uint32_t words[32];
+    WISP_CUDA_TRY(cudaMemcpy(words, L->d_last_unique, sizeof(words), cudaMemcpyDeviceToHost));
+    int n = 0;
+    for (int e = 0; e < L->E; ++e)
+        if ((words[e >> 5] >> (e & 31)) & 1u) {
+            if (n < max_ids) ids_out[n] = e;
+            ++n;
+        }
+    *n_out = n;
     return WISP_OK;
 }
 

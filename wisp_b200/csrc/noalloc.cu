@@ -13,10 +13,16 @@
 // g_static_scratch below.
 //
 // The array is sized for at most kMaxPairs (token, k) pairs, hidden size
-// kMaxHidden and intermediate size kMaxInter (about 6.3 MB); every GPU that
-// loads the library holds it until the process exits.  All calls share it
-// and it keeps the last call's contents, so calls that overlap on the GPU
-// (on different streams, or from different threads without ordering) race.
+// kMaxHidden and intermediate size kMaxInter (about 6.3 MB).  It is placed in
+// a GPU's memory when this file's device code is loaded onto that GPU, and
+// CUDA loads device code lazily (the default since CUDA 12.2): on the first
+// call on that device, not when the library is loaded.  A call with
+// num_tokens == 0 does exactly that set-up (loads the array and the code of
+// the kernels a call runs, resolves the array's address) and computes nothing, so a caller that is about to reserve the
+// free HBM makes that call first; from then on the GPU holds the array until
+// the process exits.  All calls share it and it keeps the last call's
+// contents, so calls that overlap on the GPU (on different streams, or from
+// different threads without ordering) race.
 #include <mutex>
 
 #include "common.cuh"
@@ -142,6 +148,25 @@ extern "C" int wisp_expert_compute_noalloc(int32_t device, const void *x, const 
                                            const int32_t *pair_slots, const float *topk_weights,
                                            int32_t num_tokens, int32_t top_k, int32_t hidden,
                                            int32_t inter, void *out, void *stream) {
+    if (device < 0 || device >= 64)
+        return set_error("wisp_expert_compute_noalloc: bad device"), WISP_ERR_INVALID;
+    if (num_tokens == 0) {
+        // set-up only: place the static array on `device` and resolve its address
+        int prev = -1;
+        WISP_CUDA_TRY(cudaGetDevice(&prev));
+        if (prev != device) WISP_CUDA_TRY(cudaSetDevice(device));
+        unsigned char *base = nullptr;
+        int rc = static_scratch_address(device, &base);
+        // and the code of every kernel a call launches (loading it takes device memory too)
+        cudaFuncAttributes fa;
+        if (rc == WISP_OK && cudaFuncGetAttributes(&fa, static_csr_kernel) != cudaSuccess) {
+            set_error("wisp_expert_compute_noalloc: loading the kernels failed");
+            rc = WISP_ERR_CUDA;
+        }
+        if (rc == WISP_OK) rc = preload_decode_kernels();
+        if (prev >= 0 && prev != device) cudaSetDevice(prev);
+        return rc;
+    }
     if (num_tokens < 0 || top_k < 1 || hidden <= 0 || inter <= 0 || num_slots < 1)
         return set_error("wisp_expert_compute_noalloc: bad sizes"), WISP_ERR_INVALID;
     if ((int64_t)num_tokens * top_k > kMaxPairs || hidden > kMaxHidden || inter > kMaxInter)
@@ -152,7 +177,6 @@ extern "C" int wisp_expert_compute_noalloc(int32_t device, const void *x, const 
     if (hidden % 8 || inter % 8)
         return set_error("wisp_expert_compute_noalloc: hidden and inter must be multiples of 8"),
                WISP_ERR_UNSUPPORTED;
-    if (num_tokens == 0) return WISP_OK;
     if (!x || !scratch_w13 || !scratch_w2 || !pair_slots || !topk_weights || !out)
         return set_error("wisp_expert_compute_noalloc: NULL tensor"), WISP_ERR_INVALID;
     for (const void *p : {x, scratch_w13, scratch_w2, (const void *)out})

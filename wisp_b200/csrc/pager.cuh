@@ -38,6 +38,7 @@ struct PagerParams {
     int32_t *emap;
     int64_t *hdr;        // [0] clock, [1..4] forward, miss, hits, evict; [5] groups, [6] unique experts (telemetry)
     uint32_t *slot_gen;  // [cap] page-in generation of each slot
+    uint32_t *last_unique;  // [E / 32] bitmap: unique experts of the last paged forward (or nullptr)
     // outputs (device)
     int32_t *slots;      // [T*K]
     int32_t *grp_start;  // [T+1]

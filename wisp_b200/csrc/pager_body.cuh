@@ -97,6 +97,7 @@ struct Scalars {
     long long clock, stat[4];
     int n, nm, nfree, need, G, status, err_group, mtotal, utotal, fast, nhit;
     uint32_t mask[kMaxMaskWords];
+    uint32_t umask[kMaxMaskWords];  // union of the groups' needed sets (the forward's unique experts)
 };
 
 struct Smem {
@@ -180,6 +181,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
         S.fresh[s] = 0;
     }
     for (int e = tid; e < E; e += nth) S.emap[e] = a.emap[e];
+    if (tid < kMaxMaskWords) sc.umask[tid] = 0;
     int bad = 0;
     if (S.ids) {
         for (long p = tid; p < (long)T * K; p += nth) {
@@ -257,6 +259,7 @@ static __device__ __noinline__ void pager_body(const PagerParams &a, unsigned ch
             atomicOr(&sc.mask[e >> 5], 1u << (e & 31));
         }
         __syncthreads();
+        if (tid < kMaxMaskWords) sc.umask[tid] |= sc.mask[tid];
         // ascending needed list
         if (warp == 0) {
             uint32_t w = (lane < kMaxMaskWords) ? sc.mask[lane] : 0u;
@@ -499,6 +502,10 @@ static __device__ __noinline__ void pager_finish(const PagerParams &a, unsigned 
             a.s2e[s] = S.s2e[s];
         }
         for (int e = tid; e < E; e += nth) a.emap[e] = S.emap[e];
+        // the forward's unique experts (fused_moe.py:1170-1176); a resident
+        // forward leaves them alone, as the reference's does
+        if (a.last_unique && a.count_forward && a.mode != WISP_MODE_RESIDENT && sc.status == WISP_OK)
+            for (int w = tid; w < (E + 31) / 32; w += nth) a.last_unique[w] = sc.umask[w];
         if (tid == 0) {
             a.hdr[0] = sc.clock;
             for (int i = 0; i < 4; ++i) a.hdr[1 + i] = sc.stat[i];

@@ -134,7 +134,6 @@ class WispMoEState:
         self._h = handle
         self._b13, self._b2 = b13, b2
         self.tc_min_pairs = self._query(_lib.CFG_TC_MIN_PAIRS)
-        self.last_unique_experts: set[int] = set()
         self.stats_pred_hits = 0
         self.stats_pred_total = 0
         self._refresh_views()
@@ -200,6 +199,16 @@ class WispMoEState:
     def stats(self) -> list:
         """``[forward, miss, hits, evict]``."""
         return self._read()[3]
+
+    @property
+    def last_unique_experts(self) -> set:
+        """Unique experts of the last paged forward (fused_moe.py:1170-1176);
+        a resident forward leaves it unchanged, as the reference's does."""
+        buf = (ctypes.c_int32 * self.num_experts)()
+        n = ctypes.c_int32(0)
+        _lib.check(_lib.lib().wisp_get_last_unique_experts(self._h, buf, self.num_experts, ctypes.byref(n)),
+                   "last_unique_experts")
+        return set(buf[: n.value])
 
     def _stat(i):  # noqa: N805
         def get(self):
@@ -371,13 +380,13 @@ def expert_bytes_per_cap() -> int:
 
 
 def snapshot_expert_stats(reset: bool = True) -> dict:
-    """Counters summed over layers (fused_moe.py:579-593)."""
+    """Counters summed over layers; ``ws`` = the largest unique-expert set of
+    any layer's last paged forward (fused_moe.py:579-593)."""
     miss = hit = fwd = 0
     for s in _LAYER_STATES:
         f, m, h, _e = s.stats()
         miss, hit, fwd = miss + m, hit + h, fwd + f
-    tel = [s.telemetry() for s in _LAYER_STATES]
-    ws = max((t["unique_experts"] // max(t["groups"], 1) for t in tel), default=0)
+    ws = max((len(s.last_unique_experts) for s in _LAYER_STATES), default=0)
     if reset:
         for s in _LAYER_STATES:
             s.stats_miss = 0
@@ -457,6 +466,9 @@ def _patched_process_weights_after_loading(self, layer: torch.nn.Module) -> None
     layer._wisp_state = state
     layer.w13_weight.data = torch.empty(0, dtype=cpu_w13.dtype, device=gpu)
     layer.w2_weight.data = torch.empty(0, dtype=cpu_w2.dtype, device=gpu)
+    # hand the loader's cached device blocks back so the engine's memory
+    # accounting sees only the slot scratch (fused_moe.py:906-916)
+    torch.cuda.empty_cache()
     logger.info("wisp.vllm[%s]: layer init: num_experts=%d cap_experts=%d", mode, E, state.cap_experts)
 
 
