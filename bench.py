@@ -37,25 +37,88 @@ import torch  # noqa: E402
 from wisp_b200 import workloads as wl  # noqa: E402
 
 METRIC = "decode tok/s at fixed expert-cache cap"
+
+# Benchmark workloads: model shape, decode batch per GPU,
+# expert-cache cap, layers, routing (Zipf exponent, temporal reuse).
+WORKLOADS = {
+    # one GPU; under expert parallelism `cap` stays the layer's
+    # total cache, split evenly over the GPUs (every shard pages at every N)
+    "qwen3-30b": dict(shape=wl.QWEN3_30B, batch=16, cap=32, layers=48, zipf=1.1, reuse=0.6, cap_split=True),
+    # the expert-parallel configuration, `cap` slots per GPU
+    "qwen3-235b": dict(shape=wl.QWEN3_235B, batch=64, cap=16, layers=16, zipf=1.1, reuse=0.5, cap_split=False),
+}
 SHAPE = wl.QWEN3_30B
+ZIPF, REUSE = 1.1, 0.6
 
 
 def parse():
+    global SHAPE, ZIPF, REUSE
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=24)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
-    ap.add_argument("--batch", type=int, default=16)
-    ap.add_argument("--cap", type=int, default=32)
-    ap.add_argument("--layers", type=int, default=SHAPE.layers)
+    ap.add_argument("--workload", default="qwen3-30b", choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=None, help="decode tokens per GPU (default: the workload's)")
+    ap.add_argument("--cap", type=int, default=None, help="expert-cache slots per layer (default: the workload's)")
+    ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--no-resident", action="store_true", help="skip the resident-decode phase")
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false",
+                    help="skip the other BASELINE configurations (extra keys of the line)")
     ap.add_argument("--phase", default="all", choices=["all", "resident", "prefill"],
                     help="'resident' runs only the resident-decode region (profiling: the paged "
                          "forward waits on page-ins a host thread issues during the launch, which "
                          "a kernel-serialising profiler would stall)")
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
-    return ap.parse_args()
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    SHAPE, ZIPF, REUSE = w["shape"], w["zipf"], w["reuse"]
+    for k in ("batch", "cap", "layers"):
+        if getattr(args, k) is None:
+            setattr(args, k, w[k])
+    args.cap_split = w["cap_split"]
+    return args
+
+
+def release_pinned() -> None:
+    """Hand torch's cached pinned host blocks back to the OS (expert masters
+    of a finished phase), so the next phase's masters fit the host."""
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if hasattr(torch._C, "_host_emptyCache"):
+        torch._C._host_emptyCache()
+
+
+def use_workload(name: str) -> None:
+    global SHAPE, ZIPF, REUSE
+    w = WORKLOADS[name]
+    SHAPE, ZIPF, REUSE = w["shape"], w["zipf"], w["reuse"]
+
+
+def workload_args(args, name: str, **over):
+    """A copy of ``args`` for another workload (its batch, cap and layers),
+    made current."""
+    a = argparse.Namespace(**vars(args))
+    w = WORKLOADS[name]
+    a.workload = name
+    a.batch, a.cap, a.layers, a.cap_split = w["batch"], w["cap"], w["layers"], w["cap_split"]
+    for k, v in over.items():
+        setattr(a, k, v)
+    use_workload(name)
+    return a
+
+
+def host_memory_check(nbytes: int, world: int) -> None:
+    """Refuse a run whose pinned expert masters (all ranks of this host)
+    would take more than half of the host's available memory."""
+    try:
+        with open("/proc/meminfo") as f:
+            avail = next(int(l.split()[1]) * 1024 for l in f if l.startswith("MemAvailable:"))
+    except Exception:
+        return
+    if nbytes * world > avail // 2:
+        raise SystemExit(f"bench: {nbytes * world / 1e9:.1f} GB of pinned expert masters would exceed half "
+                         f"of the host's {avail / 1e9:.1f} GB available; pass fewer --layers")
 
 
 def peaks():
@@ -169,29 +232,45 @@ def h2d_peak_gbs(dev, nbytes=1 << 30, reps=6):
     return best
 
 
-def make_masters(layers, dev):
-    """Pinned bf16 host masters per layer, N(0, 0.02) drawn on the GPU from a
-    per-layer seed (fast) and copied to pinned host memory."""
-    E, H, I = SHAPE.experts, SHAPE.hidden, SHAPE.inter
+def make_masters(layers, dev, lo=0, hi=None, shape=None):
+    """Pinned bf16 host masters of experts [lo, hi) per layer, N(0, 0.02)
+    drawn on the GPU from a per-layer seed over all E experts (so a shard is
+    the same slice of the same model at every rank count) and copied to
+    pinned host memory."""
+    shape = shape or SHAPE
+    E, H, I = shape.experts, shape.hidden, shape.inter
+    hi = E if hi is None else hi
     out = []
     for layer in range(layers):
         g = torch.Generator(device=dev).manual_seed(1000 + layer)
-        h13 = torch.empty(E, 2 * I, H, dtype=torch.bfloat16, pin_memory=True)
-        h2 = torch.empty(E, H, I, dtype=torch.bfloat16, pin_memory=True)
-        t = torch.randn(E, 2 * I, H, device=dev, generator=g, dtype=torch.float32).mul_(0.02)
-        h13.copy_(t.to(torch.bfloat16))
-        del t
-        t = torch.randn(E, H, I, device=dev, generator=g, dtype=torch.float32).mul_(0.02)
-        h2.copy_(t.to(torch.bfloat16))
-        del t
+        h13 = torch.empty(hi - lo, 2 * I, H, dtype=torch.bfloat16, pin_memory=True)
+        h2 = torch.empty(hi - lo, H, I, dtype=torch.bfloat16, pin_memory=True)
+        for e0 in range(lo, hi, 8):   # a few experts at a time: bounded device memory for large experts
+            e1 = min(hi, e0 + 8)
+            g.manual_seed(1000 + layer * 4099 + e0)
+            t = torch.randn(e1 - e0, 2 * I, H, device=dev, generator=g, dtype=torch.float32)
+            h13[e0 - lo:e1 - lo].copy_(t.mul_(0.02).to(torch.bfloat16))
+            t = torch.randn(e1 - e0, H, I, device=dev, generator=g, dtype=torch.float32)
+            h2[e0 - lo:e1 - lo].copy_(t.mul_(0.02).to(torch.bfloat16))
+            del t
         out.append((h13, h2))
     torch.cuda.synchronize()
     return out
 
 
 def routing(steps, layers, batch):
-    ids, w = wl.zipf_trace(steps, layers, batch, SHAPE.experts, SHAPE.top_k, 1.1, 0.6, seed=0)
+    ids, w = wl.zipf_trace(steps, layers, batch, SHAPE.experts, SHAPE.top_k, ZIPF, REUSE, seed=0)
     return ids, w
+
+
+def workload_name(args, world: int = 1) -> str:
+    s = f"{SHAPE.name} {args.layers}-layer expert stack, decode batch {args.batch}"
+    if world == 1:
+        return s + f", cap {args.cap}"
+    cap = args.cap // world if args.cap_split else args.cap
+    return s + (f" per GPU, expert-parallel over {world} GPUs, cap {args.cap} per layer in total "
+                f"({cap} per GPU)" if args.cap_split else
+                f" per GPU, expert-parallel over {world} GPUs, cap {cap} per GPU")
 
 
 def profile_traffic(name: str):
@@ -220,11 +299,148 @@ def dominant_kernel(batch: int, tc_min_pairs: int) -> str:
     return "batch_moe_kernel" if pairs >= tc_min_pairs else "forward_kernel"
 
 
-def algorithmic_bytes(unique_experts: int, tokens: int, launches: int) -> int:
+def algorithmic_bytes(unique_experts: int, tokens: int, launches: int, shape=None) -> int:
     """Bytes a layer forward must move (expert weights read once per group,
     activations in and out, routing ids and weights)."""
-    return (unique_experts * SHAPE.expert_bytes + tokens * SHAPE.hidden * 2 * 2
-            + tokens * SHAPE.top_k * (4 + 4)) if launches else 0
+    shape = shape or SHAPE
+    return (unique_experts * shape.expert_bytes + tokens * shape.hidden * 2 * 2
+            + tokens * shape.top_k * (4 + 4)) if launches else 0
+
+
+def paged_point(masters, dev, shape, B, C, routes, x, warmup, steps, hbm_peak, h2d, layers=None):
+    """Decode (or prefill) of a paged stack at cap C: ``routes[s][layer] =
+    (ids, w)`` on the device, ``x`` [B, H]; warm-up steps untimed, then
+    ``steps`` timed with CUDA events.  Returns the point's figures: tok/s
+    of the stack of ``layers`` layers (default: as many as masters),
+    page-in GB/s against the measured H2D peak and the step roofline (the
+    slower of the HBM bytes at the HBM peak and the page-in bytes at the H2D
+    peak, over the measured time)."""
+    from wisp_b200.integrations.vllm.fused_moe import WispMoEState
+    L = len(masters)
+    states = [WispMoEState(h13, h2, C, "paged", dev, i) for i, (h13, h2) in enumerate(masters)]
+    out = torch.empty_like(x)
+    for s in range(warmup):
+        for li in range(L):
+            states[li].forward(x, routes[s][li][1], routes[s][li][0], out=out)
+    torch.cuda.synchronize()
+    tel0 = [st.telemetry() for st in states]
+    st0 = [st.stats() for st in states]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(warmup, warmup + steps):
+        for li in range(L):
+            states[li].forward(x, routes[s][li][1], routes[s][li][0], out=out)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    for st in states:
+        st.synchronize()
+    tel1 = [st.telemetry() for st in states]
+    st1 = [st.stats() for st in states]
+    for st in states:
+        st.close()
+    d = {k: sum(t1[k] - t0[k] for t0, t1 in zip(tel0, tel1)) for k in tel0[0]}
+    T = x.shape[0]
+    pb = d["pagein_bytes"]
+    hb = algorithmic_bytes(d["unique_experts"], T * L * steps, d["kernel_launches"], shape)
+    sec = ms * 1e-3
+    stack = layers or L
+    return {"tok_s": T * steps / sec * L / stack, "ms_per_layer_step": ms / (steps * L),
+            "pagein_gbs": pb / sec / 1e9, "pagein_frac_of_h2d_peak": pb / sec / 1e9 / h2d,
+            "step_roofline_frac": max(hb / (hbm_peak * 1e9), pb / (h2d * 1e9)) / sec,
+            "misses": sum(x1[1] - x0[1] for x0, x1 in zip(st0, st1)),
+            "hits": sum(x1[2] - x0[2] for x0, x1 in zip(st0, st1)),
+            "launches": d["kernel_launches"], "layers_timed": L, "stack_layers": stack, "steps": steps}
+
+
+def one_gpu_235b(args, dev, hbm_peak, h2d):
+    """configs[4]'s layer shape and routing on one GPU: all 128 experts of
+    each layer paged at 16 slots, decode batch 64, the workload's layers."""
+    a = workload_args(args, "qwen3-235b")
+    s = SHAPE
+    host_memory_check(a.layers * s.experts * s.expert_bytes, 1)
+    mm = make_masters(a.layers, dev, shape=s)
+    steps, warm = 3, 2
+    tids, tw = wl.zipf_trace(warm + steps, a.layers, a.batch, s.experts, s.top_k, ZIPF, REUSE, seed=0)
+    routes = [[(torch.from_numpy(tids[t, li]).to(dev), torch.from_numpy(tw[t, li]).to(dev))
+               for li in range(a.layers)] for t in range(warm + steps)]
+    x = wl.hidden_states(a.batch, s.hidden, seed=0).to(dev)
+    r = paged_point(mm, dev, s, a.batch, a.cap, routes, x, warm, steps, hbm_peak, h2d)
+    r["workload"] = workload_name(a, 1)
+    del mm
+    release_pinned()
+    return r
+
+
+def sweep_phase(masters, dev, hbm_peak, h2d):
+    """Every BASELINE configuration besides the headline, one line each:
+    configs[0] (one Qwen3-30B-A3B layer, 256 decode tokens at batch 1, cap 8,
+    routed on the GPU from Zipf-biased logits), configs[1] at batch 1/4/16 x
+    cap 8/16/24/32 (the 48-layer stack), configs[2] (a paged prefill chunk
+    at cap 32, uniform top-8: every group pages) and configs[3] (Mixtral-8x7B
+    decode at batch 1/8, cap 2/4).  Stacks longer than the layers timed
+    report tok/s scaled by layer count (each layer pages its own cache)."""
+    from wisp_b200.integrations.vllm.fused_moe import select_experts
+    q = wl.QWEN3_30B
+    out = {}
+    # configs[0]
+    logits = wl.router_logits(256, q.experts, seed=0).to(dev)
+    w, ids = select_experts(logits, q.top_k)
+    x256 = wl.hidden_states(256, q.hidden, seed=0).to(dev)
+    from wisp_b200.integrations.vllm.fused_moe import WispMoEState
+    st = WispMoEState(masters[0][0], masters[0][1], 8, "paged", dev, 0)
+    o = torch.empty((1, q.hidden), dtype=torch.bfloat16, device=dev)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tel0 = st.telemetry()
+    a.record()
+    for t in range(256):
+        st.forward(x256[t:t + 1], w[t:t + 1], ids[t:t + 1], out=o)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    tel1 = st.telemetry()
+    f, miss, hits, ev = st.stats()
+    st.close()
+    pb = tel1["pagein_bytes"] - tel0["pagein_bytes"]
+    out["cfg0_layer_b1_cap8"] = {"tok_s_one_layer": 256 / (ms * 1e-3), "us_per_token": ms * 1e3 / 256,
+                                 "pagein_gbs": pb / (ms * 1e-3) / 1e9,
+                                 "pagein_frac_of_h2d_peak": pb / (ms * 1e-3) / 1e9 / h2d,
+                                 "misses": miss, "hits": hits, "evictions": ev, "forwards": f}
+    # configs[1] sweep
+    L = len(masters)
+    for B in (1, 4, 16):
+        steps, warm = 3, 2
+        tids, tw = wl.zipf_trace(warm + steps, L, B, q.experts, q.top_k, 1.1, 0.6, seed=11 + B)
+        routes = [[(torch.from_numpy(tids[s, li]).to(dev), torch.from_numpy(tw[s, li]).to(dev))
+                   for li in range(L)] for s in range(warm + steps)]
+        x = wl.hidden_states(B, q.hidden, seed=B).to(dev)
+        for C in (8, 16, 24, 32):
+            out[f"cfg1_b{B}_cap{C}"] = paged_point(masters, dev, q, B, C, routes, x, warm, steps, hbm_peak, h2d)
+    # configs[2]: prefill chunks of 2048 tokens per sequence, batch 1 and 4, cap 32
+    for B, nl in ((1, 2), (4, 1)):
+        T = 2048 * B
+        tids, tw = wl.uniform_topk(T, q.experts, q.top_k, seed=40 + B)
+        routes = [[(torch.from_numpy(tids).to(dev), torch.from_numpy(tw).to(dev)) for _ in range(nl)]]
+        x = wl.hidden_states(T, q.hidden, seed=7).to(dev)
+        r = paged_point(masters[:nl], dev, q, T, 32, routes, x, 0, 1, hbm_peak, h2d, layers=q.layers)
+        r["prefill_tok_s"] = r.pop("tok_s")
+        out[f"cfg2_prefill_b{B}_t2048_cap32"] = r
+    # configs[3]: Mixtral-8x7B, 4 of its 32 layers timed
+    m = wl.MIXTRAL_8X7B
+    mm = make_masters(4, dev, shape=m)
+    for B in (1, 8):
+        steps, warm = 3, 2
+        tids, tw = wl.zipf_trace(warm + steps, 4, B, m.experts, m.top_k, 0.8, 0.0, seed=21 + B)
+        routes = [[(torch.from_numpy(tids[s, li]).to(dev), torch.from_numpy(tw[s, li]).to(dev))
+                   for li in range(4)] for s in range(warm + steps)]
+        x = wl.hidden_states(B, m.hidden, seed=B).to(dev)
+        for C in (2, 4):
+            out[f"cfg3_mixtral_b{B}_cap{C}"] = paged_point(mm, dev, m, B, C, routes, x, warm, steps, hbm_peak,
+                                                           h2d, layers=m.layers)
+    del mm
+    release_pinned()
+    return out
 
 
 def run_wisp(args):
@@ -239,6 +455,7 @@ def run_wisp(args):
     if args.phase == "prefill":
         return prefill_only(args, dev, hbm_peak, peak_src)
     t0 = time.time()
+    host_memory_check(L * SHAPE.experts * SHAPE.expert_bytes, 1)
     masters = make_masters(L, dev)
     states = [WispMoEState(h13, h2, C, "paged", dev, i) for i, (h13, h2) in enumerate(masters)]
     ids_np, w_np = routing(total, L, B)
@@ -330,9 +547,21 @@ def run_wisp(args):
     torch.cuda.empty_cache()
     res = {}
     if not args.no_resident:
-        for rb in sorted({B, 1}, reverse=True):
+        for rb in sorted({B, 4, 1}, reverse=True):
             res[f"batch{rb}"] = resident_phase(args, masters, dev, hbm_peak, rb)
+    sweep = None
+    if args.sweep and args.workload == "qwen3-30b":
+        t_sw = time.time()
+        sweep = sweep_phase(masters, dev, hbm_peak, h2d)
+        sweep["wall_s"] = time.time() - t_sw
     del masters
+    release_pinned()
+    if sweep is not None:
+        # configs[4]'s shapes on one GPU (the same-shape line of the expert-parallel runs)
+        t_sw = time.time()
+        sweep["qwen3_235b_one_gpu"] = one_gpu_235b(args, dev, hbm_peak, h2d)
+        sweep["qwen3_235b_one_gpu"]["wall_s"] = time.time() - t_sw
+        use_workload(args.workload)
 
     roofline = None
     if res:
@@ -350,17 +579,19 @@ def run_wisp(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded Zipf routing trace; random-init N(0,0.02) weights)",
-        "config": {"workload": f"qwen3-30b-a3b {L}-layer expert stack, decode batch {B}, cap {C}",
+        "config": {"workload": workload_name(args),
                    "layers": L, "batch": B, "cap": C, "experts": SHAPE.experts,
                    "top_k": SHAPE.top_k, "hidden": SHAPE.hidden, "inter": SHAPE.inter,
-                   "routing": "zipf1.1 reuse0.6", "l2": "inputs larger than L2 (each step reads "
-                   "every layer's routed experts, >= 48 x 8 x 9.4 MB, from HBM)"},
+                   "routing": f"zipf{ZIPF} reuse{REUSE}", "l2": "inputs larger than L2 (each step reads "
+                   f"every layer's routed experts, >= {L} x {SHAPE.top_k} x {SHAPE.expert_bytes / 1e6:.1f} MB, "
+                   "from HBM)"},
         "gpu_launches": launches,
         "roofline": roofline,
         "step_roofline": step_roof,
         "pagein": {"gbs": pagein_gbs, "h2d_peak_gbs": h2d, "frac": pagein_gbs / h2d,
                    "misses": misses, "hits": hits, "bytes": pagein_bytes},
         "resident_decode": res,
+        "configs": sweep,
         "e2e": e2e,
         "clocks": clk.summary(),
         "setup_s": setup_s,
@@ -376,7 +607,7 @@ def resident_only(args, dev, hbm_peak, peak_src):
             "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": r["us_per_forward"] * r["layers"] / 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"qwen3-30b-a3b {r['layers']}-layer expert stack, resident decode "
+            "config": {"workload": f"{SHAPE.name} {r['layers']}-layer expert stack, resident decode "
                                    f"batch {args.batch}"},
             "gpu_launches": r["launches"],
             "roofline": {"bound": "hbm", "kernel": r["kernel"], "achieved": r["hbm_gbs"],
@@ -435,7 +666,7 @@ def prefill_only(args, dev, hbm_peak, peak_src):
     return {"metric": "prefill tok/s (resident, 2048-token chunk)", "value": T * args.steps / (ms * 1e-3 / L) / L,
             "unit": "tok/s per layer stack of %d" % L, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic (uniform top-8 routing)",
-            "config": {"workload": f"qwen3-30b-a3b prefill, {L} resident layers, T {T}, uniform top-8"},
+            "config": {"workload": f"{SHAPE.name} prefill, {L} resident layers, T {T}, uniform top-{SHAPE.top_k}"},
             "prefill": {"us_per_layer": us, "tflops": tf, "tflops_peak": tflops_peak,
                         "tensor_frac": tf / tflops_peak, "weight_gbs": gbs, "hbm_peak_gbs": hbm_peak,
                         "hbm_frac": gbs / hbm_peak, "roofline_us": roof_us, "roofline_frac": roof_us / us,
@@ -494,51 +725,33 @@ def resident_phase(args, masters, dev, hbm_peak, batch):
             "hbm_gbs": gbs, "hbm_peak_gbs": hbm_peak, "frac": gbs / hbm_peak}
 
 
-def make_shard_masters(layers, dev, rank, world):
-    """Pinned bf16 host masters of this rank's experts per layer: the same
-    N(0, 0.02) weights as make_masters (same per-layer seeds), sliced to the
-    shard, so the whole model is identical at every rank count."""
-    E = SHAPE.experts
-    lo, hi = rank * E // world, (rank + 1) * E // world
-    out = []
-    for layer in range(layers):
-        g = torch.Generator(device=dev).manual_seed(1000 + layer)
-        t = torch.randn(E, 2 * SHAPE.inter, SHAPE.hidden, device=dev, generator=g, dtype=torch.float32)
-        h13 = t[lo:hi].mul_(0.02).to(torch.bfloat16).cpu().pin_memory()
-        del t
-        t = torch.randn(E, SHAPE.hidden, SHAPE.inter, device=dev, generator=g, dtype=torch.float32)
-        h2 = t[lo:hi].mul_(0.02).to(torch.bfloat16).cpu().pin_memory()
-        del t
-        out.append((h13, h2))
-    torch.cuda.synchronize()
-    return out
-
-
 def run_wisp_ep(args):
     """Expert-parallel stack over the torchrun ranks (one GPU each): rank r owns
     experts [r E/P, (r+1) E/P) of every layer in its own pinned memory and
-    pages them into cap = min(--cap, E/P) slots per layer; each rank decodes its
-    own batch of --batch tokens (weak scaling: global batch = P x batch),
-    tokens exchanged by NCCL all-to-all.  Times are CUDA events, max over ranks."""
-    import datetime
-
+    pages them into its own slots; each rank decodes its own batch of --batch
+    tokens (weak scaling: global batch = P x batch); the (token, k) rows move
+    over peer memory (EPExchange).  For the default workload the layer's
+    expert cache stays --cap slots in total, split evenly over the GPUs, so
+    every shard pages at every P (the same fraction of each shard cached);
+    for qwen3-235b --cap is per GPU.  Times are CUDA events, max
+    over ranks."""
     import torch.distributed as dist
-    from wisp_b200.expert_parallel import EPMoELayer
+    from wisp_b200.expert_parallel import EPExchange, EPMoELayer
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
-    torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     L, B = args.layers, args.batch
     E = SHAPE.experts
     per = E // world
-    C = min(args.cap, per)
+    C = max(2, min(args.cap // world if args.cap_split else args.cap, per))
     total = args.warmup + args.steps
     t0 = time.time()
-    masters = make_shard_masters(L, dev, rank, world)
-    # a cap that holds the whole shard makes it resident (primed once; the
-    # one-launch forward), otherwise the shard pages
+    host_memory_check(L * per * SHAPE.expert_bytes, world)
+    lo, hi = rank * per, (rank + 1) * per
+    masters = make_masters(L, dev, lo, hi)
+    # a cap that holds the whole shard makes it resident (primed once)
     mode = "resident" if C == per else "paged"
-    layers = [EPMoELayer(h13, h2, E, C, mode, dev, i) for i, (h13, h2) in enumerate(masters)]
+    exchange = EPExchange(SHAPE.hidden, B * SHAPE.top_k, dev)
+    layers = [EPMoELayer(h13, h2, E, C, mode, dev, i, exchange=exchange) for i, (h13, h2) in enumerate(masters)]
     ids_all, w_all = routing(total, L, B * world)
     ids_d = torch.from_numpy(np.ascontiguousarray(ids_all[:, :, rank * B:(rank + 1) * B])).to(dev)
     w_d = torch.from_numpy(np.ascontiguousarray(w_all[:, :, rank * B:(rank + 1) * B])).to(dev)
@@ -554,13 +767,14 @@ def run_wisp_ep(args):
         step(s, x_d, w_d, ids_d, out_d)
     torch.cuda.synchronize()
     for lay in layers:
-        lay.local.synchronize()
+        lay.synchronize()
     tel0 = [lay.local.telemetry() for lay in layers]
+    ex0 = exchange.launches
     dist.barrier()
+    torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(list(range(world)), enabled=rank == 0)
     with clk:
-        torch.cuda.synchronize()
         ev0.record()
         for s in range(args.warmup, total):
             step(s, x_d, w_d, ids_d, out_d)
@@ -568,15 +782,14 @@ def run_wisp_ep(args):
         torch.cuda.synchronize()
     dist.barrier()
     for lay in layers:
-        lay.local.synchronize()
+        lay.synchronize()
     tel1 = [lay.local.telemetry() for lay in layers]
 
     def delta(key):
         return sum(b[key] - a[key] for a, b in zip(tel0, tel1))
 
-    # per forward: route + pack + combine kernels of the exchange, plus the shard's own launches
     stats = torch.tensor([ev0.elapsed_time(ev1), float(delta("pagein_bytes")),
-                          float(delta("kernel_launches") + 3 * L * args.steps),
+                          float(delta("kernel_launches") + exchange.launches - ex0),
                           float(delta("unique_experts"))], dtype=torch.float64, device=dev)
     mx = stats.clone()
     dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -593,6 +806,7 @@ def run_wisp_ep(args):
     e2e_steps = min(args.steps, 8)
     torch.cuda.synchronize()
     dist.barrier()
+    torch.cuda.synchronize()
     ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev2.record()
     for j in range(e2e_steps):
@@ -609,23 +823,29 @@ def run_wisp_ep(args):
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     for lay in layers:
         lay.close()
+    exchange.close()
+    del masters
+    release_pinned()
     dist.barrier()
-    dist.destroy_process_group()
     h2d = h2d_peak_gbs(dev) if rank == 0 else 0.0
     pagein_gbs = float(stats[1]) / (ms * 1e-3) / 1e9
+    steps_layers = args.steps * L
     return {
         "metric": METRIC, "value": world * B * args.steps / (ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded Zipf routing trace; random-init N(0,0.02) weights)",
-        "config": {"workload": f"qwen3-30b-a3b {L}-layer expert stack, expert-parallel over {world} GPUs, "
-                               f"decode batch {B} per GPU, cap {C} per GPU",
+        "config": {"workload": workload_name(args, world),
                    "layers": L, "batch_per_gpu": B, "global_batch": B * world, "cap_per_gpu": C,
-                   "experts_per_gpu": per, "shard_mode": mode, "parallelism": f"ep{world}",
-                   "routing": "zipf1.1 reuse0.6",
+                   "cap_per_layer_total": C * world, "experts_per_gpu": per, "shard_mode": mode,
+                   "parallelism": f"ep{world}", "exchange": "peer memory (CUDA IPC over NVLink), no collective",
+                   "routing": f"zipf{ZIPF} reuse{REUSE}",
                    "l2": "inputs larger than L2 (each step reads every layer's routed experts from HBM)"},
         "gpu_launches": int(stats[2]),
         "roofline": None,
+        "per_gpu": {"pagein_bytes_per_layer_step": float(stats[1]) / world / steps_layers,
+                    "unique_experts_per_layer_step": float(stats[3]) / world / steps_layers,
+                    "ms_per_layer_step": ms / steps_layers},
         "pagein": {"gbs_all_ranks": pagein_gbs, "h2d_peak_gbs_per_gpu": h2d,
                    "frac_of_per_gpu_peak_x_gpus": pagein_gbs / (h2d * world) if h2d else None,
                    "bytes": float(stats[1])},
@@ -640,46 +860,69 @@ def run_wisp_ep(args):
 
 
 def run_reference(args):
-    """CPU restatement of the reference path on the host cores (bounded sample)."""
-    from oracle.moe import moe_reference  # noqa: F401
+    """The reference path restated for the host cores, timed on a bounded
+    sample: per layer and decode step, the reference's first-fit sub-batching
+    and LRU pager (oracle/pager.py, bit-exact with fused_moe.py:264-358 and
+    :1102-1168), each page-in a host copy into that layer's scratch slot (the
+    reference's H2D copy), and vLLM fused_experts' arithmetic per group: each
+    resident expert once over all of the group's tokens routed to it (bf16
+    GEMMs with fp32 accumulation, h and a stored bf16, y = (W2 a) * w stored
+    bf16), then the routing-order sum over k.  All host threads; the sampled
+    layers' mean time per layer is scaled to the workload's layer count."""
     from oracle.pager import PagerOracle, first_fit_groups
     n = len(os.sched_getaffinity(0))
     torch.set_num_threads(n)
     L, B, C = args.layers, args.batch, args.cap
-    E, H, I = SHAPE.experts, SHAPE.hidden, SHAPE.inter
-    sample_layers = 2
-    g = torch.Generator().manual_seed(0)
-    masters = [((torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16),
-                (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16))
-               for _ in range(sample_layers)]
+    E, H, I, K = SHAPE.experts, SHAPE.hidden, SHAPE.inter, SHAPE.top_k
+    sample_layers = max(1, min(4, L))
+    masters = []
+    for li in range(sample_layers):
+        # one expert's N(0, 0.02) weights copied to every expert: the values do
+        # not change the time, and drawing every expert on the CPU takes minutes
+        g = torch.Generator().manual_seed(1000 + li)
+        w13 = torch.empty(E, 2 * I, H, dtype=torch.bfloat16)
+        w2 = torch.empty(E, H, I, dtype=torch.bfloat16)
+        b13 = (torch.randn(2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+        b2 = (torch.randn(H, I, generator=g) * 0.02).to(torch.bfloat16)
+        for e in range(E):
+            w13[e].copy_(b13)
+            w2[e].copy_(b2)
+        masters.append((w13, w2))
     scratch = [(torch.empty(C, 2 * I, H, dtype=torch.bfloat16), torch.empty(C, H, I, dtype=torch.bfloat16))
                for _ in range(sample_layers)]
     pagers = [PagerOracle(E, C) for _ in range(sample_layers)]
-    # a trace long enough for the time-bounded sample (config 2 decodes 512 tokens)
-    n_trace = args.warmup + max(args.steps, 512)
+    n_trace = args.warmup + max(args.steps, 128)   # the sample wraps around it
     ids_np, w_np = routing(n_trace, sample_layers, B)
-    x = wl.hidden_states(B, H, seed=0).float()
+    x = wl.hidden_states(B, H, seed=0)
+    silu = torch.nn.functional.silu
 
     def layer_fwd(li, s):
+        s = args.warmup + (s - args.warmup) % (n_trace - args.warmup) if s >= n_trace else s
         ids = ids_np[s, li]
         w = torch.from_numpy(w_np[s, li])
         p = pagers[li]
         p.stats_forward += 1
-        out = torch.zeros(B, H)
+        out = torch.empty(B, H, dtype=torch.bfloat16)
         for t0, t1 in first_fit_groups(ids, C):
             rec = p.ensure_resident(ids[t0:t1])
             for e, slot in rec.placed:
                 scratch[li][0][slot].copy_(masters[li][0][e])
                 scratch[li][1][slot].copy_(masters[li][1][e])
-            for t in range(t0, t1):
-                acc = torch.zeros(H)
-                for k in range(ids.shape[1]):
-                    slot = p.expert_to_slot[int(ids[t, k])]
-                    h = (scratch[li][0][slot].float() @ x[t]).to(torch.bfloat16).float()
-                    a = (torch.nn.functional.silu(h[:I]) * h[I:]).to(torch.bfloat16).float()
-                    y = ((scratch[li][1][slot].float() @ a) * w[t, k]).to(torch.bfloat16).float()
-                    acc += y
-                out[t] = acc
+            gid = torch.from_numpy(ids[t0:t1].astype(np.int64))
+            y = torch.empty(t1 - t0, K, H, dtype=torch.bfloat16)
+            for e in torch.unique(gid).tolist():
+                rows, cols = (gid == e).nonzero(as_tuple=True)
+                slot = p.expert_to_slot[e]
+                h = x[t0 + rows] @ scratch[li][0][slot].T                      # bf16 out, fp32 accumulate
+                a = (silu(h[:, :I].float()).to(torch.bfloat16).float() * h[:, I:].float()).to(torch.bfloat16)
+                y[rows, cols] = ((a @ scratch[li][1][slot].T).float()
+                                 * w[t0 + rows, cols].unsqueeze(1)).to(torch.bfloat16)
+            acc = y[:, 0].float()
+            for k in range(1, K):
+                acc = acc + y[:, k].float()
+                if K <= 4:
+                    acc = acc.to(torch.bfloat16).float()
+            out[t0:t1] = acc.to(torch.bfloat16)
         return out
 
     for s in range(min(args.warmup, 2)):
@@ -693,14 +936,15 @@ def run_reference(args):
             layer_fwd(li, s)
         done += 1
         s += 1
-        if time.perf_counter() - t0 > args.cpu_sample_s or s >= n_trace:
+        if time.perf_counter() - t0 > args.cpu_sample_s:
             break
     dt = time.perf_counter() - t0
     per_layer = dt / (done * sample_layers)
     tok_s = B / (per_layer * L)
     return {"value": tok_s, "unit": "tok/s", "cores": n, "kind": "port",
-            "sample": f"{done} decode steps x {sample_layers} layers (of {L}) at batch {B}, cap {C}; "
-                      f"tok/s extrapolated to {L} layers ({dt:.1f} s of CPU work)"}
+            "sample": f"{done} decode steps x {sample_layers} layers (of {L}) at batch {B}, cap {C}: each "
+                      f"expert computed once per token group (bf16 GEMMs, fp32 accumulation); tok/s = batch / "
+                      f"(mean time per layer x {L}) ({dt:.1f} s of CPU work)"}
 
 
 def main():
@@ -713,8 +957,7 @@ def main():
         line = {"metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "impl": "reference",
-                "data": "synthetic", "config": {"workload": f"qwen3-30b-a3b {args.layers}-layer "
-                                                f"expert stack, decode batch {args.batch}, cap {args.cap}"},
+                "data": "synthetic", "config": {"workload": workload_name(args, args.gpus)},
                 "cpu_baseline": cpu,
                 "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -722,7 +965,19 @@ def main():
         return
     world = int(os.environ.get("WORLD_SIZE", 1))
     if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
         line = run_wisp_ep(args)
+        if args.sweep and args.workload == "qwen3-30b":
+            # configs[4] (the expert-parallel configuration) at this GPU count
+            line["configs"] = {"ep_qwen3_235b": run_wisp_ep(workload_args(args, "qwen3-235b", steps=3, warmup=2))}
+            use_workload("qwen3-30b")
+        dist.barrier()
+        dist.destroy_process_group()
         if rank == 0:
             print(json.dumps(line))
         return

@@ -84,6 +84,19 @@ WISP_API int wisp_moe_forward(wisp_layer *layer, const void *x, const float *top
                      int32_t top_k, void *out, void *stream);
 
 /*
+ * Router for callers that hold router logits: per token, fp32 softmax over
+ * the num_experts logits (fp32, or bf16 when logits_bf16), the top_k largest
+ * probabilities in descending order (ties to the lower expert id) and, when
+ * renormalize, the weights divided by their sum -- the routing the reference's
+ * paged forward takes from vLLM's select_experts (fused_moe.py:1054-1076).
+ * topk_weights [T][k] fp32, topk_ids [T][k] int32; asynchronous on `stream`.
+ * num_experts <= 1024, top_k <= 32.
+ */
+WISP_API int wisp_route_topk(const void *logits, int32_t logits_bf16, int32_t num_tokens, int32_t num_experts,
+                             int32_t top_k, int32_t renormalize, float *topk_weights, int32_t *topk_ids,
+                             void *stream);
+
+/*
  * One LRU admission step for an arbitrary id list, with page-in, finished
  * before returning.  Replaces WispMoEState.ensure_resident
  * (fused_moe.py:264-358).
@@ -100,6 +113,20 @@ WISP_API int wisp_ensure_resident(wisp_layer *layer, const void *ids, int32_t id
  */
 WISP_API int wisp_pager_step(wisp_layer *layer, const void *topk_ids, int32_t ids_int64,
                              int32_t num_tokens, int32_t top_k, int32_t *slots_out, void *stream);
+
+/*
+ * Speculative page-in of predicted experts: the reference's
+ * WispMoEState.prefetch_async (fused_moe.py:360-433), bit-exact.  predicted
+ * (host, n <= E ids) in the order the caller iterates its predicted set.
+ * Experts with no slot are loaded, in that order; victims are taken by LRU
+ * (tick, slot) among slots whose expert is neither predicted nor in the
+ * layer's last forward's unique set; a prediction larger than the free slots
+ * plus those victims is loaded in part; the clock moves only when something
+ * loads; evictions count, misses and hits do not.  The state changes and the
+ * page-ins run on the layer's copy stream after its last forward, and its
+ * next forward waits for them.  Returns once the copies are issued.
+ */
+WISP_API int wisp_prefetch_async(wisp_layer *layer, const int32_t *predicted, int32_t n, void *stream);
 
 /* Resident mode: identity map and full copy.  fused_moe.py:242-258 (cap == E). */
 WISP_API int wisp_prime_identity(wisp_layer *layer, void *stream);
@@ -229,33 +256,68 @@ WISP_API int wisp_expert_compute_noalloc(int32_t device, const void *x, const vo
 /*
  * Expert parallelism (no counterpart in the reference, which runs one GPU per
  * layer).  Rank r of `world` owns experts [r * experts_per_rank,
- * (r + 1) * experts_per_rank) and pages only those; the (token, k) pairs go
- * to their owners by NCCL all-to-all, each owner runs wisp_moe_forward on the
- * rows it received (top_k 1, local expert ids), and the weighted rows come
- * back for the combine.
- *
- * wisp_ep_dispatch: from x [T][H] bf16, topk_ids [T][k] (int32, or int64 when
- * ids_int64), topk_weights [T][k] fp32, writes the send buffers in owner
- * order (pairs of one owner keep their (t, k) order): send_x [T*k][H] bf16,
- * send_meta [T*k][2] int32 = (local expert id, weight bits), send_counts
- * [world + 1] int64 = rows per owner, then the number of ids outside
- * [0, world * experts_per_rank) (non-zero: nothing else is valid), and
- * pair_pos [T*k] int32 = the send row of pair t*k+j.  Asynchronous on
- * `stream`; hidden a multiple of 8, world <= 64.
+ * (r + 1) * experts_per_rank) and pages only those.  The (token, k) pairs go
+ * to their owners over peer memory (NVLink / NVSwitch): each rank's group
+ * holds one region with the same layout on every rank, mapped into every
+ * peer through CUDA IPC, and the kernels below store rows straight into the
+ * peer's region (plain stores; no collective library on the data path).
+ * Per layer forward every rank calls, in this order:
+ *   wisp_ep_dispatch   route the call's pairs and store their rows and
+ *                      records into the owners' receive segments;
+ *   wisp_ep_receive    wait for every source, compact the received rows
+ *                      (by run of same-class sources, by local expert
+ *                      within a run) into the group's x_recv / ids_recv /
+ *                      w_recv and return the counts to the host;
+ *   the owner's own wisp_moe_forward on x_recv[0:R] (top_k 1, local ids)
+ *   into y_recv[0:R];
+ *   wisp_ep_return     store each weighted row back into its source;
+ *   wisp_ep_combine    wait for every owner and write out[t] = the
+ *                      routing-order sum of the token's k rows (the one-GPU
+ *                      combine, so the output is byte-identical to a one-GPU
+ *                      layer whose compute takes the same kernels).
+ * Each dispatch starts a new epoch; every wait is bounded (default 10 s,
+ * wisp_ep_group_config) and a wait that runs out is reported, never hangs.
  */
-WISP_API int wisp_ep_dispatch(const void *x, const void *topk_ids, int32_t ids_int64,
-                              const float *topk_weights, int32_t num_tokens, int32_t top_k,
-                              int32_t hidden, int32_t experts_per_rank, int32_t world, void *send_x,
-                              int32_t *send_meta, int64_t *send_counts, int32_t *pair_pos,
-                              void *stream);
+typedef struct wisp_ep_group wisp_ep_group;
 
-/*
- * wisp_ep_combine: out[t] = sum over j in routing order of y_back[pair_pos[t*k+j]]
- * (fp32, stored bf16) -- the routing-order sum of the one-GPU forward, so the
- * result is byte-identical to it.  y_back [T*k][H] bf16 in send order.
- */
-WISP_API int wisp_ep_combine(const void *y_back, const int32_t *pair_pos, int32_t num_tokens,
-                             int32_t top_k, int32_t hidden, void *out, void *stream);
+/* This rank's exchange buffers for calls of at most max_pairs (token, k)
+ * pairs per rank and hidden size `hidden` (a multiple of 8). */
+WISP_API int wisp_ep_group_create(int32_t rank, int32_t world, int32_t device, int32_t max_pairs,
+                                  int32_t hidden, wisp_ep_group **out);
+/* The 64-byte CUDA IPC handle of this rank's region (to all-gather). */
+WISP_API int wisp_ep_group_ipc_handle(wisp_ep_group *group, void *handle_out);
+/* Map every peer's region: handles = world consecutive 64-byte handles, by rank. */
+WISP_API int wisp_ep_group_connect(wisp_ep_group *group, const void *handles);
+/* Ranks emulated in one process on one device: groups[r] is rank r's group. */
+WISP_API int wisp_ep_group_connect_local(wisp_ep_group *group, wisp_ep_group *const *groups);
+WISP_API int wisp_ep_group_destroy(wisp_ep_group *group);
+/* Device addresses of the owner-side buffers: x_recv [world*max_pairs][H]
+ * bf16, ids_recv int32, w_recv fp32, y_recv [world*max_pairs][H] bf16. */
+WISP_API int wisp_ep_group_buffers(wisp_ep_group *group, void **x_recv, void **ids_recv, void **w_recv,
+                                   void **y_recv);
+/* Limit of one device-side wait of this group's kernels (nanoseconds). */
+WISP_API int wisp_ep_group_config(wisp_ep_group *group, int64_t wait_ns);
+/* x [T][H] bf16, topk_ids [T][k] int32 (int64 when ids_int64), topk_weights
+ * [T][k] fp32; asynchronous on `stream`.  An id outside [0, world *
+ * experts_per_rank) makes every rank's wisp_ep_receive fail alike. */
+WISP_API int wisp_ep_dispatch(wisp_ep_group *group, const void *x, const void *topk_ids, int32_t ids_int64,
+                              const float *topk_weights, int32_t num_tokens, int32_t top_k,
+                              int32_t experts_per_rank, void *stream);
+/* Synchronous: returns when the received rows are compacted.  A run is a
+ * maximal range of consecutive sources (rank order, sources with rows) of one
+ * compute class -- sources of at least class_min_pairs (token, k) pairs form
+ * one class (0: a single class); rows keep their run and are ordered by local
+ * expert within it, stably.  counts_out / src_pairs_out (host, [world], may
+ * be NULL): rows from each source and each source's pair count; total_out:
+ * rows received. */
+WISP_API int wisp_ep_receive(wisp_ep_group *group, int32_t class_min_pairs, void *stream, int32_t *counts_out,
+                             int32_t *src_pairs_out, int32_t *total_out);
+/* Store y_recv[0:R] (R of the last receive) back into the sources. */
+WISP_API int wisp_ep_return(wisp_ep_group *group, void *stream);
+/* out [T][H] bf16 = routing-order sum of this rank's returned rows. */
+WISP_API int wisp_ep_combine(wisp_ep_group *group, int32_t num_tokens, int32_t top_k, void *out, void *stream);
+/* Wait for the device and report (then clear) a failure of the group's kernels. */
+WISP_API int wisp_ep_sync(wisp_ep_group *group);
 
 #ifdef __cplusplus
 }

@@ -7,6 +7,7 @@ Follows, in order of the reference source:
   * ``ensure_resident``:               fused_moe.py:264-358
   * ``prime_identity``:                fused_moe.py:242-258
   * ``resize_cap``:                    fused_moe.py:439-490
+  * ``prefetch_async``:                fused_moe.py:360-433
   * first-fit token sub-batching and the per-forward call sequence of
     ``_wisp_forward_cuda_paged``:      fused_moe.py:1017, 1102-1168
 
@@ -94,6 +95,51 @@ class PagerOracle:
             rec.placed.append((e, slot))
         for e in needed_set:
             self.lru_tick[self.expert_to_slot[e]] = self.lru_clock
+        return rec
+
+    # fused_moe.py:360-433
+    def prefetch_async(self, predicted, last_unique) -> StepRecord:
+        """Speculative load of ``predicted`` (an iterable in the order the
+        reference iterates its set) with the history bias: slots holding an
+        expert of ``last_unique`` or of the prediction are not victims; a
+        prediction larger than the free slots plus the victims is cut short;
+        the clock moves only when something loads; evictions count, misses
+        do not."""
+        predicted = list(predicted)
+        pred_set = set(predicted)
+        last = set(last_unique)
+        rec = StepRecord(predicted, [], [], [])
+        to_load = [e for e in predicted if e not in self.expert_to_slot]
+        if not to_load:
+            return rec
+        free_slots = [s for s in range(self.cap) if self.slot_to_expert[s] == -1]
+        cands = sorted(((self.lru_tick[s], s) for s in range(self.cap)
+                        if self.slot_to_expert[s] != -1
+                        and self.slot_to_expert[s] not in last
+                        and self.slot_to_expert[s] not in pred_set),
+                       key=lambda x: x[0])
+        need_slot = len(to_load) - len(free_slots)
+        if need_slot > 0:
+            if need_slot > len(cands):
+                to_load = to_load[: len(cands) + len(free_slots)]
+                need_slot = len(to_load) - len(free_slots)
+            for _tick, s in cands[:need_slot]:
+                ev = self.slot_to_expert[s]
+                self.expert_to_slot.pop(ev, None)
+                self.slot_to_expert[s] = -1
+                free_slots.append(s)
+                self.stats_evict += 1
+                rec.victims.append((s, ev))
+        self.lru_clock += 1
+        for e in to_load:
+            if not free_slots:
+                break
+            slot = free_slots.pop()
+            self.slot_to_expert[slot] = int(e)
+            self.expert_to_slot[int(e)] = slot
+            self.lru_tick[slot] = self.lru_clock
+            rec.placed.append((int(e), slot))
+        rec.missing = [e for e, _ in rec.placed]
         return rec
 
     # fused_moe.py:242-258

@@ -1,13 +1,14 @@
-"""Expert-parallel host logic on CPU: gloo ranks run EPMoELayer's real
-collective sequence (counts, rows, records, results) with the CUDA route /
-pack / combine kernels and the expert compute replaced by torch stand-ins.
+"""Expert-parallel host logic on CPU: gloo ranks run EPMoELayer's forward
+(dispatch, receive, the per-class local calls, return, combine) with the
+peer-memory exchange replaced by a stand-in that moves the same rows and
+records with gloo all-to-alls, and the expert compute by a torch stand-in.
 
 Checks the combine against a direct computation, the order in which each
 owner receives its rows ((source rank, pair) order, local ids), that an
-expert id out of range on one rank raises on every rank with no collective
-left waiting, and that sources of different call sizes have their rows
-computed in their own classes (one local call per run of same-class
-sources, each forced to its class, the size rule restored after)."""
+expert id out of range on one rank raises on every rank with nothing left
+waiting, and that sources of different call sizes have their rows computed
+in their own classes (one local call per run of same-class sources, each
+forced to its class, the size rule restored after)."""
 import os
 import socket
 
@@ -32,6 +33,9 @@ class _FakeExperts:
     def compute_class(self, pairs):
         return "tc" if pairs >= 10 else "cuda"
 
+    def class_threshold(self):
+        return 10
+
     def configure(self, compute_class=None):
         self.classes.append(compute_class)
 
@@ -40,32 +44,92 @@ class _FakeExperts:
         g = ids.reshape(-1).long() + self.rank * self.per
         out.copy_((x.float() * (g + 1).view(-1, 1).float() * w.reshape(-1, 1)).to(torch.bfloat16))
 
+    def synchronize(self):
+        pass
 
-class _CpuEP(EPMoELayer):
-    """The route/pack and combine kernels restated in torch (CPU tensors)."""
 
-    def _route_pack(self, x, w, ids, T_, K_, H_, send_x, send_meta, counts, pos):
+class _GlooExchange:
+    """The peer-memory exchange's four steps restated with gloo collectives
+    on CPU tensors: same rows, records, order and combine arithmetic."""
+
+    def __init__(self, rank, world):
+        self.rank, self.world, self.hidden = rank, world, H
+
+    def dispatch(self, x, w, ids, e_local):
         flat = ids.reshape(-1).long()
-        bad = int(((flat < 0) | (flat >= self.num_experts)).sum())
-        counts[self.world] = bad
-        if bad:
-            counts[: self.world] = 0
-            pos.fill_(-1)
-            return
-        dest = flat // self.experts_per_rank
-        order = torch.argsort(dest, stable=True)
-        pos[order] = torch.arange(flat.numel(), dtype=torch.int32)
-        send_x.copy_(x[order // K_])
-        send_meta[:, 0] = (flat - dest * self.experts_per_rank)[order].to(torch.int32)
-        send_meta[:, 1] = w.reshape(-1)[order].view(torch.int32)
-        counts[: self.world] = torch.bincount(dest, minlength=self.world)
+        self.T, self.K = ids.shape
+        P = flat.numel()
+        bad = bool(((flat < 0) | (flat >= e_local * self.world)).any())
+        owner = flat // e_local
+        send_rows, send_recs, counts = [], [], []
+        for d in range(self.world):
+            sel = (owner == d).nonzero().reshape(-1) if not bad else torch.empty(0, dtype=torch.long)
+            counts.append(-1 if bad else int(sel.numel()))
+            send_rows.append(x[sel // self.K].float())
+            send_recs.append(torch.stack([(flat[sel] - d * e_local).float(), w.reshape(-1)[sel].float(),
+                                          sel.float()], dim=1) if len(sel) else torch.zeros(0, 3))
+        head = torch.tensor([[c, P] for c in counts], dtype=torch.int64)
+        rhead = torch.empty_like(head)
+        dist.all_to_all_single(rhead, head)
+        self.counts = [int(v) for v in rhead[:, 0]]
+        self.src_pairs = [int(v) for v in rhead[:, 1]]
+        ok = all(c >= 0 for c in self.counts)
+        scount = [max(c, 0) for c in counts]
+        rcount = [max(c, 0) for c in self.counts]
+        rows = torch.empty((sum(rcount), H))
+        recs = torch.empty((sum(rcount), 3))
+        dist.all_to_all_single(rows, torch.cat(send_rows) if sum(scount) else torch.empty(0, H), rcount, scount)
+        dist.all_to_all_single(recs, torch.cat(send_recs) if sum(scount) else torch.empty(0, 3), rcount, scount)
+        self.ok, self.rows, self.recs, self.scount, self.rcount = ok, rows, recs, scount, rcount
 
-    def _combine(self, back, pos, T_, K_, out):
-        acc = torch.zeros((T_, back.shape[1]), dtype=torch.float32)
-        p = pos.view(T_, K_).long()
+    def receive(self, class_min_pairs=0):
+        if not self.ok:
+            raise _lib.WispError(_lib.WISP_ERR_BAD_EXPERT, "a rank routed an expert id out of range")
+        R = sum(self.rcount)
+        # runs of consecutive same-class sources; rows ordered by expert within a run, stably
+        order, row, prev = [], 0, None
+        for c, pairs in zip(self.rcount, self.src_pairs):
+            cls = class_min_pairs > 0 and pairs >= class_min_pairs
+            if c and (prev is None or cls != prev):
+                order.append([row, row + c])
+                prev = cls
+            elif c:
+                order[-1][1] += c
+            row += c
+        perm = torch.cat([r0 + torch.argsort(self.recs[r0:r1, 0], stable=True) for r0, r1 in order]) \
+            if order else torch.empty(0, dtype=torch.long)
+        self.perm = perm
+        self.rows, self.recs_sorted = self.rows[perm], self.recs[perm]
+        self.x = self.rows.to(torch.bfloat16)
+        self.ids = self.recs_sorted[:, 0].to(torch.int32).reshape(R, 1)
+        self.w = self.recs_sorted[:, 1].reshape(R, 1).contiguous()
+        self.y = torch.empty((R, H), dtype=torch.bfloat16)
+        return self.counts, self.src_pairs
+
+    def received(self, R):
+        return self.x[:R], self.w[:R], self.ids[:R], self.y[:R]
+
+    def send_back(self):
+        back = torch.empty((sum(self.scount), H))
+        y = torch.empty_like(self.y)
+        y[self.perm] = self.y                       # back to (source, pair) order
+        dist.all_to_all_single(back, y.float(), self.scount, self.rcount)
+        pairs = torch.empty((sum(self.scount), 3))
+        dist.all_to_all_single(pairs, self.recs, self.scount, self.rcount)
+        self.back = torch.zeros((self.T * self.K, H))
+        self.back[pairs[:, 2].long()] = back
+
+    def combine(self, out, T_, K_):
+        acc = torch.zeros((T_, H))
+        b = self.back.view(T_, K_, H)
         for k in range(K_):
-            acc += back[p[:, k]].float()
+            acc = acc + b[:, k]
+            if K_ <= 4:
+                acc = acc.to(torch.bfloat16).float()
         out.copy_(acc.to(torch.bfloat16))
+
+    def synchronize(self):
+        pass
 
 
 def _routing(rank, seed):
@@ -83,26 +147,29 @@ def _worker(rank, world, port):
     try:
         per = E // world
         local = _FakeExperts(rank, per)
-        layer = _CpuEP(None, None, E, per, local=local, device="cpu")
+        layer = EPMoELayer(None, None, E, per, local=local, device="cpu", exchange=_GlooExchange(rank, world))
         for seed in range(3):
             x, w, ids = _routing(rank, seed)
             out = layer.forward(x, w, ids)
-            # direct: sum over k in routing order of the bf16 rows
+            # direct: sum over k in routing order of the bf16 rows (bf16 partial sums: top-3)
             acc = torch.zeros((T, H))
             for k in range(K):
                 y = (x.float() * (ids[:, k].long() + 1).view(-1, 1).float() * w[:, k:k + 1]).to(torch.bfloat16)
-                acc += y.float()
+                acc = (acc + y.float()).to(torch.bfloat16).float()
             assert torch.equal(out, acc.to(torch.bfloat16)), f"rank {rank} seed {seed}: combine differs"
-            # this owner saw every source's pairs for it, sources in rank order, pairs in (t, k) order
+            # this owner saw every source's pairs for it (one run: every source has 15
+            # pairs), ordered by local expert, stably
             expect = []
             for src in range(world):
                 _, _, sids = _routing(src, seed)
                 flat = sids.reshape(-1).long()
                 mine = flat[(flat // per) == rank]
                 expect.append(mine - rank * per)
-            seen = local.seen[-1] if len(torch.cat(expect)) else torch.empty(0, dtype=torch.int32)
-            assert torch.equal(seen.long(), torch.cat(expect)), f"rank {rank}: receive order"
-            if len(torch.cat(expect)):
+            expect = torch.cat(expect)
+            expect = expect[torch.argsort(expect, stable=True)]
+            seen = local.seen[-1] if len(expect) else torch.empty(0, dtype=torch.int32)
+            assert torch.equal(seen.long(), expect), f"rank {rank}: receive order"
+            if len(expect):
                 # every source called with T * K = 15 pairs: one call, forced to that
                 # class, then back to the size rule
                 assert local.classes[-2:] == ["tc", "auto"], local.classes
@@ -127,7 +194,7 @@ def _free_port():
 
 
 @pytest.mark.parametrize("world", [2, 4])
-def test_ep_collectives_gloo(world):
+def test_ep_host_logic_gloo(world):
     mp.start_processes(_worker, args=(world, _free_port()), nprocs=world, start_method="spawn")
 
 
@@ -142,7 +209,7 @@ def _mixed_worker(rank, world, port):
         per = E // world
         Ts = [5, 4, 3, 2][:world]   # x K = 3: 15, 12 pairs ("tc"); 9, 6 ("cuda")
         local = _FakeExperts(rank, per)
-        layer = _CpuEP(None, None, E, per, local=local, device="cpu")
+        layer = EPMoELayer(None, None, E, per, local=local, device="cpu", exchange=_GlooExchange(rank, world))
         g = torch.Generator().manual_seed(7 + rank)
         T = Ts[rank]
         ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).to(torch.int32)
@@ -151,7 +218,8 @@ def _mixed_worker(rank, world, port):
         out = layer.forward(x, w, ids)
         acc = torch.zeros((T, H))
         for k in range(K):
-            acc += (x.float() * (ids[:, k].long() + 1).view(-1, 1).float() * w[:, k:k + 1]).to(torch.bfloat16).float()
+            y = (x.float() * (ids[:, k].long() + 1).view(-1, 1).float() * w[:, k:k + 1]).to(torch.bfloat16)
+            acc = (acc + y.float()).to(torch.bfloat16).float()
         assert torch.equal(out, acc.to(torch.bfloat16)), f"rank {rank}: combine differs"
         # what this owner received from each source, and the calls it made
         counts = torch.zeros(world, dtype=torch.int64)

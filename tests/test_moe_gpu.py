@@ -95,23 +95,32 @@ def test_byte_identical_across_caps_and_placements():
     del g
 
 
-def test_qwen3_layer_config1_decode_parity():
-    """Config 1: Qwen3-30B-A3B layer (H 2048, I 768, E 128, top-8), logits
-    routing with the Zipf bias, cap 8, decode at batch 1; 24 tokens checked
-    against the oracle, then byte-compared with a resident layer."""
+def test_qwen3_layer_config1_decode_parity(golden):
+    """Config 1: Qwen3-30B-A3B layer (H 2048, I 768, E 128, top-8), router
+    logits with the Zipf bias, cap 8, decode at batch 1, all 256 tokens.  The
+    routing runs on the GPU from the logits (select_experts); its ids equal
+    the ones the reference's pager trace was recorded with; every output is
+    checked against the oracle, the pager state against the reference's
+    recorded trace, then the outputs are byte-compared with a resident layer."""
+    from wisp_b200.integrations.vllm.fused_moe import select_experts
     shape = wl.QWEN3_30B
     w13, w2 = wl.layer_weights(shape, 0)
-    T = 24
-    w, ids = wl.logits_routing(T, shape.experts, shape.top_k, seed=0)
+    T = 256
+    logits = wl.router_logits(T, shape.experts, seed=0)
     x = wl.hidden_states(T, shape.hidden, seed=0)
+    w_d, ids_d = select_experts(logits.to(DEV), shape.top_k)
+    w, ids = w_d.cpu(), ids_d.cpu()
+    case = golden["cfg1_b1_cap8"]
+    assert np.array_equal(ids.numpy(), case["ids"].reshape(T, shape.top_k))
     st = state(w13, w2, 8)
     outs = [fwd(st, x[t:t + 1], w[t:t + 1], ids[t:t + 1]) for t in range(T)]
     out = torch.cat(outs)
     ref = moe_reference(x, w13, w2, w, ids)
     c = compare(out, ref)
     assert c["max_abs"] <= MAX_ABS and c["mean_rel"] <= MEAN_REL, c
-    f, miss, hits, ev = st.stats()
-    assert f == T and miss > 0 and ev > 0
+    s2e, tick, clock, stats = st._read()
+    assert s2e == case["s2e"][-1].tolist() and tick == case["tick"][-1].tolist()
+    assert clock == int(case["clock"][-1]) and stats == case["stats"][-1].tolist()
     st.close()
     res = state(w13, w2, shape.experts, "resident")
     out_res = torch.cat([fwd(res, x[t:t + 1], w[t:t + 1], ids[t:t + 1]) for t in range(T)])

@@ -46,8 +46,10 @@ SIGNATURES = {
                                          _vp, _vp, _c_int32, _c_int32, ctypes.POINTER(_vp)]),
     "wisp_layer_destroy": (ctypes.c_int, [_vp]),
     "wisp_moe_forward": (ctypes.c_int, [_vp, _vp, _pf, _vp, _c_int32, _c_int32, _c_int32, _vp, _vp]),
+    "wisp_route_topk": (ctypes.c_int, [_vp, _c_int32, _c_int32, _c_int32, _c_int32, _c_int32, _vp, _vp, _vp]),
     "wisp_ensure_resident": (ctypes.c_int, [_vp, _vp, _c_int32, _c_int32, _vp]),
     "wisp_pager_step": (ctypes.c_int, [_vp, _vp, _c_int32, _c_int32, _c_int32, _vp, _vp]),
+    "wisp_prefetch_async": (ctypes.c_int, [_vp, _p32, _c_int32, _vp]),
     "wisp_prime_identity": (ctypes.c_int, [_vp, _vp]),
     "wisp_resize_cap": (ctypes.c_int, [_vp, _c_int32, _vp]),
     "wisp_get_state": (ctypes.c_int, [_vp, _p32, _p64, _p64, _p64, _p32, _p32]),
@@ -62,9 +64,20 @@ SIGNATURES = {
     "wisp_layer_query": (ctypes.c_int, [_vp, _c_int32, ctypes.POINTER(_c_int64)]),
     "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,
                                                    _c_int32, _c_int32, _c_int32, _c_int32, _vp, _vp]),
-    "wisp_ep_dispatch": (ctypes.c_int, [_vp, _vp, _c_int32, _vp, _c_int32, _c_int32, _c_int32, _c_int32,
-                                        _c_int32, _vp, _vp, _vp, _vp, _vp]),
-    "wisp_ep_combine": (ctypes.c_int, [_vp, _vp, _c_int32, _c_int32, _c_int32, _vp, _vp]),
+    "wisp_ep_group_create": (ctypes.c_int, [_c_int32, _c_int32, _c_int32, _c_int32, _c_int32,
+                                            ctypes.POINTER(_vp)]),
+    "wisp_ep_group_ipc_handle": (ctypes.c_int, [_vp, _vp]),
+    "wisp_ep_group_connect": (ctypes.c_int, [_vp, _vp]),
+    "wisp_ep_group_connect_local": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    "wisp_ep_group_destroy": (ctypes.c_int, [_vp]),
+    "wisp_ep_group_buffers": (ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                                             ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    "wisp_ep_group_config": (ctypes.c_int, [_vp, _c_int64]),
+    "wisp_ep_dispatch": (ctypes.c_int, [_vp, _vp, _vp, _c_int32, _vp, _c_int32, _c_int32, _c_int32, _vp]),
+    "wisp_ep_receive": (ctypes.c_int, [_vp, _c_int32, _vp, _p32, _p32, _p32]),
+    "wisp_ep_return": (ctypes.c_int, [_vp, _vp]),
+    "wisp_ep_combine": (ctypes.c_int, [_vp, _c_int32, _c_int32, _vp, _vp]),
+    "wisp_ep_sync": (ctypes.c_int, [_vp]),
 }
 
 

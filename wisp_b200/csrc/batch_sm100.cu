@@ -111,6 +111,8 @@ struct Args {
     const int32_t *u_slot;      // [nu]
     const int32_t *nu_dev;
     const int32_t *pager_status;
+    const int32_t *u_gen;       // [nu] generation each expert's slot must reach before its loads, or nullptr
+    const uint32_t *slot_ready; // [slots] generation landed in each slot
     // in-kernel routing (route == true)
     int route;
     const void *ids;
@@ -252,6 +254,25 @@ __device__ __forceinline__ bool wait_ready(const Args &g, int word_index, uint32
         }
     }
     fence_proxy_async_global();  // the rows (generic-proxy stores) before the TMA reads
+    return true;
+}
+
+// Producer wait until expert u's slot holds the generation its page-in
+// writes (the copy stream raises slot_ready after the copies).
+__device__ __forceinline__ bool wait_slot(const Args &g, int u, int slot, volatile int *abort) {
+    const uint32_t need = (uint32_t)g.u_gen[u];
+    if (need == 0) return true;
+    const uint32_t *word = g.slot_ready + slot;
+    const volatile uint32_t *abort_all = g.ready + kAbortWord;
+    if (ld_acquire_gpu(word) < need) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (ld_acquire_gpu(word) < need) {
+            if (*abort || *abort_all) return false;
+            if ((long long)(globaltimer_ns() - t0) > g.wait_ns) return false;
+            __nanosleep(64);
+        }
+    }
+    fence_proxy_async_global();  // the copy engine's writes before the TMA reads
     return true;
 }
 
@@ -468,6 +489,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     for (int b = threadIdx.x; b < L.nblocks; b += blockDim.x) {
+        if (g.u_gen) {
+            // experts still paging in: the pager's list order (resident experts
+            // first, then the misses in page-in order), so tiles meet their
+            // slots in the order the copies land
+            L.order[b] = (int16_t)b;
+            continue;
+        }
         const int rb = L.rows[b];
         int rank = 0;
         for (int c = 0; c < L.nblocks; ++c) {
@@ -563,6 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     a0 = slot * 2 * I + tl.col * kWM;
                     a1 = a0 + I;
                     kbc = H / kBK;
+                    if (g.u_gen && !wait_slot(g, u, slot, abort)) {
+                        give_up(R, g);
+                        break;
+                    }
                     if (g.route && !gathered) {
                         if (!wait_ready(g, kGatheredWord, gridDim.x, abort)) {
                             give_up(R, g);
@@ -795,6 +827,8 @@ int launch_batch_group(const PrefillGroup &p, const BatchCounters &c, cudaStream
     a.u_slot = p.u_slot;
     a.nu_dev = p.nu_dev;
     a.pager_status = p.pager_status;
+    a.u_gen = p.u_gen;
+    a.slot_ready = p.slot_ready;
     rc = gemm::launch_gather(p, stream);
     if (!rc) rc = launch_kernel(p, a, p.nu, stream);
     return rc;

@@ -121,6 +121,10 @@ struct wisp_layer {
     int64_t *d_tick = nullptr, *d_hdr = nullptr;
     uint32_t *d_slot_gen = nullptr, *d_slot_ready = nullptr;
     uint32_t *d_last_unique = nullptr;  // bitmap of the last paged forward's unique experts
+    uint32_t h_last_unique[32] = {};    // host copy, valid when the host read the last forward's mailbox
+    bool last_unique_host = false;
+    int32_t *h_pf = nullptr, *d_pf = nullptr;  // prefetch: predicted ids [E], then status / records (mapped)
+    cudaEvent_t ev_pf = nullptr;
     unsigned int *d_bar = nullptr;
     unsigned int *d_flow = nullptr;  // forward-kernel dataflow words (kFlowWords)
     int kparity = 0;                 // parity of the forward-kernel launches
@@ -541,6 +545,10 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
     WISP_CUDA_TRY(cudaEventRecord(L->ev_pager, stream));
     WISP_CUDA_TRY(cudaEventSynchronize(L->ev_pager));
     const int status = ((volatile int32_t *)L->h_mb)[0];
+    if (status == WISP_OK && count_forward && L->mode != WISP_MODE_RESIDENT) {
+        for (int w = 0; w < 32; ++w) L->h_last_unique[w] = (uint32_t)((volatile int32_t *)L->h_mb)[kMbUnique + w];
+        L->last_unique_host = true;
+    }
     if (status == WISP_ERR_OVERFLOW)
         return fail(WISP_ERR_OVERFLOW,
                     "wisp: per-kernel-call working set exceeds cap_experts (" +
@@ -581,6 +589,8 @@ PrefillGroup tc_group(const wisp_layer *L, const void *x, const float *w, void *
     pg.u_slot = L->d_u_slot + p0;
     pg.nu_dev = L->d_grp_nu + g;
     pg.pager_status = pager_status;
+    pg.u_gen = nullptr;
+    pg.slot_ready = L->d_slot_ready;
     pg.nu = nu_bound;
     pg.npairs = (t1 - t0) * K;
     pg.t0 = t0;
@@ -650,6 +660,10 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
             wait_g = std::max(wait_g, (int)rec[kMbRec * mi + 3]);
             ++mi;
         }
+        // the weight-stationary kernel waits inside for each expert's slot (its
+        // resident experts compute while the misses stream in); every other
+        // kernel waits for the group's copies on the stream
+        const bool slot_waits = compute && path == Path::kBatchTC && t1 > t0 && nu[g] > 0;
         if (mi > m0) {
             if (wait_g >= 0) WISP_CUDA_TRY(cudaStreamWaitEvent(L->copy_stream, L->ev_group[wait_g], 0));
             for (int m = m0; m < mi; ++m) {
@@ -657,11 +671,13 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
                 if (rc) return rc;
             }
             WISP_CUDA_TRY(cudaEventRecord(L->ev_copy[g], L->copy_stream));
-            WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copy[g], 0));
+            if (!slot_waits) WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copy[g], 0));
         }
         if (compute && t1 > t0 && nu[g] > 0 && path != Path::kDecode) {
             // tensor-core kernels (gather, gate-up + SiLU-mul, down, combine)
-            rc = launch_tc_group(L, path, tc_group(L, x, w, out, g, t0, t1, K, nu[g], nullptr), stream);
+            PrefillGroup pg = tc_group(L, x, w, out, g, t0, t1, K, nu[g], nullptr);
+            if (slot_waits && mi > m0) pg.u_gen = L->d_u_gen + (int64_t)t0 * K;
+            rc = launch_tc_group(L, path, pg, stream);
             if (rc) return rc;
         } else if (compute && t1 > t0 && nu[g] > 0) {
             const int64_t p0 = (int64_t)t0 * K;
@@ -800,6 +816,7 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
         L->mb_busy[slot].store(1);
     }
     fp.pg.mb = L->d_mb + (long)slot * L->mb_words;
+    if (paged) L->last_unique_host = false;  // this forward's set is known on the device only
     WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));  // the workspace, whichever stream used it last
     WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
     int rc = launch_forward(fp, T, stream);
@@ -894,7 +911,11 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
         cudaStreamCreateWithFlags(&L->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&L->ev_pager, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&L->ev_copies, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&L->ev_last, cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&L->ev_last, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&L->ev_pf, cudaEventDisableTiming) != cudaSuccess ||
+        cudaHostAlloc(&L->h_pf, sizeof(int32_t) * ((size_t)num_experts + kMbRec * (num_experts + 1)),
+                      cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer((void **)&L->d_pf, L->h_pf, 0) != cudaSuccess)
         return bail(fail(WISP_ERR_CUDA, "wisp_layer_create: buffer/stream/event setup failed"));
     *L->h_done = 0;
     *L->h_status = 0;
@@ -935,6 +956,8 @@ int wisp_layer_destroy(wisp_layer *L) {
     if (L->h_done) cudaFreeHost(L->h_done);
     if (L->h_status) cudaFreeHost(L->h_status);
     if (L->h_flag_ring) cudaFreeHost(L->h_flag_ring);
+    if (L->h_pf) cudaFreeHost(L->h_pf);
+    if (L->ev_pf) cudaEventDestroy(L->ev_pf);
     for (auto e : L->ev_group) cudaEventDestroy(e);
     for (auto e : L->ev_copy) cudaEventDestroy(e);
     for (cudaEvent_t e : {L->ev_pager, L->ev_copies, L->ev_last})
@@ -1013,6 +1036,54 @@ int wisp_pager_step(wisp_layer *L, const void *topk_ids, int32_t ids_int64, int3
     if (slots_out && num_tokens > 0)
         WISP_CUDA_TRY(cudaMemcpy(slots_out, L->d_slots, sizeof(int32_t) * (size_t)num_tokens * top_k,
                                  cudaMemcpyDeviceToHost));
+    return WISP_OK;
+}
+
+int wisp_prefetch_async(wisp_layer *L, const int32_t *predicted, int32_t n, void *stream) {
+    if (!L) return fail(WISP_ERR_INVALID, "wisp_prefetch_async: NULL layer");
+    if (n < 0 || n > L->E || (n > 0 && !predicted))
+        return fail(WISP_ERR_INVALID, "wisp_prefetch_async: n must be in [0, num_experts]");
+    if (L->mode != WISP_MODE_PAGED) return fail(WISP_ERR_INVALID, "wisp_prefetch_async: layer is not paged");
+    (void)stream;
+    std::lock_guard<std::mutex> lk(L->mu);
+    DeviceGuard guard(L->dev);
+    int rc = take_errors(L);
+    if (rc) return rc;
+    if (n == 0) return WISP_OK;
+    std::copy(predicted, predicted + n, L->h_pf);
+    int32_t *out = L->h_pf + L->E;
+    out[0] = -1;
+    PrefetchParams p{};
+    p.pred = L->d_pf;
+    p.n = n;
+    p.E = L->E;
+    p.cap = L->cap;
+    p.s2e = L->d_s2e;
+    p.tick = L->d_tick;
+    p.emap = L->d_emap;
+    p.hdr = L->d_hdr;
+    p.slot_gen = L->d_slot_gen;
+    p.last_unique = L->d_last_unique;
+    p.out = L->d_pf + L->E;
+    // on the copy stream, after this layer's last forward is done with its
+    // slots and state; the next forward's pager waits for these copies
+    WISP_CUDA_TRY(cudaStreamWaitEvent(L->copy_stream, L->ev_last, 0));
+    rc = launch_prefetch(p, L->copy_stream);
+    if (rc) return rc;
+    ++L->launches;
+    WISP_CUDA_TRY(cudaEventRecord(L->ev_pf, L->copy_stream));
+    WISP_CUDA_TRY(cudaEventSynchronize(L->ev_pf));
+    const volatile int32_t *vo = out;
+    if (vo[0] == WISP_ERR_BAD_EXPERT)
+        return fail(WISP_ERR_BAD_EXPERT, "wisp_prefetch_async: predicted id outside [0, " + std::to_string(L->E) + ")");
+    if (vo[0] != WISP_OK) return fail(WISP_ERR_CUDA, "wisp_prefetch_async: prefetch kernel did not report");
+    const int nload = vo[1];
+    for (int i = 0; i < nload; ++i) {
+        const volatile int32_t *r = out + kMbRec * (i + 1);
+        rc = issue_pagein(L, r[0], r[1], (uint32_t)r[2]);
+        if (rc) return rc;
+    }
+    WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
     return WISP_OK;
 }
 
@@ -1153,9 +1224,13 @@ int wisp_get_last_unique_experts(wisp_layer *L, int32_t *ids_out, int32_t max_id
         return fail(WISP_ERR_INVALID, "wisp_get_last_unique_experts: bad argument");
     std::lock_guard<std::mutex> lk(L->mu);
     DeviceGuard guard(L->dev);
-    WISP_CUDA_TRY(cudaDeviceSynchronize());
     uint32_t words[32];
-    WISP_CUDA_TRY(cudaMemcpy(words, L->d_last_unique, sizeof(words), cudaMemcpyDeviceToHost));
+    if (L->last_unique_host) {
+        std::copy(L->h_last_unique, L->h_last_unique + 32, words);
+    } else {
+        WISP_CUDA_TRY(cudaDeviceSynchronize());
+        WISP_CUDA_TRY(cudaMemcpy(words, L->d_last_unique, sizeof(words), cudaMemcpyDeviceToHost));
+    }
     int n = 0;
     for (int e = 0; e < L->E; ++e)
         if ((words[e >> 5] >> (e & 31)) & 1u) {

@@ -12,11 +12,13 @@ namespace wisp {
 // reads, so the pager never overwrites a mailbox under the reader:
 //   [0] status  [1] groups G  [2] misses  [3] failing group  [4] sum of unique experts
 //   [5] forward-kernel status (slot 0 only)  [6] reserved  [7] sequence number (written last)
+//   [kMbUnique ...]            32 words: bitmap of the forward's unique experts
 //   [kMbHeader ...]            group first tokens, G+1 entries (last = T)
 //   [kMbHeader + T + 1 ...]    unique experts per group, G entries
 //   [mailbox_miss_offset(T)..] page-in records of kMbRec words:
 //                              {expert, slot, group, wait_group, generation, 0, 0, 0}
-constexpr int kMbHeader = 8;
+constexpr int kMbUnique = 8;
+constexpr int kMbHeader = kMbUnique + 32;
 constexpr int kMbRec = 8;
 inline __host__ __device__ long mailbox_miss_offset(int T) {
     return ((kMbHeader + 2L * T + 1 + 7) / 8) * 8;
@@ -55,6 +57,23 @@ struct PagerParams {
 
 size_t pager_smem_bytes(int E, int cap, int T, int K);
 int launch_pager(const PagerParams &p, cudaStream_t stream);
+
+// Speculative page-in of predicted experts (the reference's prefetch_async,
+// fused_moe.py:360-433) on the layer's state; one CTA.  `out` (mapped host
+// memory): [0] status, [1] experts to load, then kMbRec words per load
+// {expert, slot, generation, 0...}.
+struct PrefetchParams {
+    const int32_t *pred;          // [n] predicted ids, in the order the caller iterates its set
+    int n, E, cap;
+    int32_t *s2e;
+    int64_t *tick;
+    int32_t *emap;
+    int64_t *hdr;                 // [0] clock, [4] evictions
+    uint32_t *slot_gen;
+    const uint32_t *last_unique;  // [E / 32] the layer's last forward's unique experts
+    int32_t *out;
+};
+int launch_prefetch(const PrefetchParams &p, cudaStream_t stream);
 // The pager is run by one whole CTA of kPagerThreads threads (pager_body.cuh).
 constexpr int kPagerThreads = 256;
 

@@ -517,6 +517,7 @@ static __device__ __noinline__ void pager_finish(const PagerParams &a, unsigned 
         int *mb_grp = a.mb + kMbHeader;
         int *mb_nu = mb_grp + (T + 1);
         const int G = sc.status == WISP_OK ? sc.G : 0;
+        for (int w = tid; w < kMaxMaskWords; w += nth) a.mb[kMbUnique + w] = (int)sc.umask[w];
         for (int g = tid; g <= G; g += nth) mb_grp[g] = S.grp[g];
         for (int g = tid; g < G; g += nth) mb_nu[g] = a.grp_nu[g];
         __syncthreads();

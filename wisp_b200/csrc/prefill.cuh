@@ -17,6 +17,9 @@ struct PrefillGroup {
     const int32_t *u_slot;          // [nu]
     const int32_t *nu_dev;          // experts in the group (device word written by the pager)
     const int32_t *pager_status;    // pager status (device); nullptr when the host checked it
+    const int32_t *u_gen;           // [nu] page-in generation each expert's slot must reach (0: resident
+                                    // before the call), or nullptr: the slots are ready at launch
+    const uint32_t *slot_ready;     // [slots] generation landed in each slot (written by the copy stream)
     int nu, npairs;                 // nu: upper bound of *nu_dev (grid sizes)
     int t0, t1, K, H, I;
     const float *topk_w;            // [T * K]

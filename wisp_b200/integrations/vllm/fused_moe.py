@@ -263,6 +263,19 @@ class WispMoEState:
             _lib.stream_ptr(torch.cuda.current_stream(self.device))), "pager_step")
         return slots
 
+    def prefetch_async(self, predicted_experts) -> None:
+        """Speculative page-in of ``predicted_experts`` (fused_moe.py:360-433):
+        loads the predicted experts that have no slot, in the order the set
+        iterates, evicting by LRU among slots whose expert is neither predicted
+        nor in :attr:`last_unique_experts`; a prediction larger than the room
+        loads in part.  Runs on the layer's copy stream after its last forward;
+        its next forward waits for the copies."""
+        ids = [int(e) for e in predicted_experts]
+        if not ids:
+            return
+        arr = (ctypes.c_int32 * len(ids))(*ids)
+        _lib.check(_lib.lib().wisp_prefetch_async(self._h, arr, len(ids), None), "prefetch_async")
+
     def resize_cap(self, new_cap: int) -> None:
         """Hot resize at a drained barrier (fused_moe.py:439-490); refreshes the
         scratch views."""
@@ -294,6 +307,13 @@ class WispMoEState:
             "wisp_moe_forward")
         return out
 
+    def forward_logits(self, x: torch.Tensor, router_logits: torch.Tensor, top_k: int,
+                       renormalize: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The forward from router logits: softmax top-k routing on the GPU
+        (:func:`select_experts`, fused_moe.py:1054-1076), then :meth:`forward`."""
+        w, ids = select_experts(router_logits, top_k, renormalize)
+        return self.forward(x, w, ids, out=out)
+
     def synchronize(self) -> None:
         """Wait for this layer's queued forwards (kernels and page-ins) and raise
         the first error any of them hit (forwards return before their work runs)."""
@@ -322,6 +342,15 @@ class WispMoEState:
             return "cuda"
         return "tc" if pairs >= min(self.tc_min_pairs, _lib.PREFILL_MIN_PAIRS) else "cuda"
 
+    def class_threshold(self) -> int:
+        """Calls of at least this many (token, k) pairs compute on the tensor
+        cores (0: every call on the CUDA-core kernels); the rule of
+        :meth:`compute_class`."""
+        h, i = self.hidden_size, self.intermediate_size
+        if not (h > 0 and i > 0 and h % 256 == 0 and i % 128 == 0):
+            return 0
+        return min(self.tc_min_pairs, _lib.PREFILL_MIN_PAIRS)
+
     def configure(self, *, asynchronous: bool | None = None, wait_ns: int | None = None,
                   drop_pageins: int | None = None, tc_min_pairs: int | None = None,
                   compute_class: str | None = None) -> None:
@@ -346,6 +375,26 @@ class WispMoEState:
             self.tc_min_pairs = self._query(_lib.CFG_TC_MIN_PAIRS)
 
 
+def select_experts(router_logits: torch.Tensor, top_k: int, renormalize: bool = True):
+    """Softmax top-k routing on the GPU (``wisp_route_topk``): fp32 softmax
+    over the experts, the ``top_k`` largest probabilities in descending order
+    (ties to the lower id), renormalised to sum to one when ``renormalize`` --
+    the Qwen3 / Mixtral routing of the reference's paged forward
+    (fused_moe.py:1054-1076).  router_logits [T, E] fp32 or bf16 on a CUDA
+    device; returns (topk_weights [T, k] fp32, topk_ids [T, k] int32)."""
+    logits = router_logits.contiguous()
+    if logits.dtype not in (torch.float32, torch.bfloat16):
+        logits = logits.float()
+    T, E = logits.shape
+    w = torch.empty((T, top_k), dtype=torch.float32, device=logits.device)
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=logits.device)
+    _lib.check(_lib.lib().wisp_route_topk(
+        logits.data_ptr(), int(logits.dtype == torch.bfloat16), T, E, int(top_k), int(bool(renormalize)),
+        w.data_ptr(), ids.data_ptr(), _lib.stream_ptr(torch.cuda.current_stream(logits.device))),
+        "wisp_route_topk")
+    return w, ids
+
+
 # ---------------------------------------------------------------------------
 # Runtime config and layer registry (fused_moe.py:497-526, 537-593)
 # ---------------------------------------------------------------------------
@@ -353,6 +402,74 @@ class WispMoEState:
 _WISP_RUNTIME_CONFIG: dict[str, Any] = {"mode": _Mode.RESIDENT, "cap_experts_override": None}
 _LAYER_STATES: list[WispMoEState] = []
 _LAYER_BY_ID: dict[int, WispMoEState] = {}
+
+# Cross-layer prefetch (off unless WISP_PREFETCH is set, as in the reference):
+# the co-occurrence table (None: not loaded yet; False: disabled after a load
+# failure) and the current decode step's observations, layer -> unique experts.
+_COOCCUR_TABLE: Any = None
+_CURRENT_STEP_OBS: dict[int, set] = {}
+
+
+def _env_on(name: str) -> bool:
+    return os.environ.get(name, "0").strip().lower() in ("1", "true", "yes")
+
+
+def _maybe_load_cooccur():
+    """The co-occurrence table: ``WISP_COOCCUR_PATH`` (a warm table in the
+    reference's JSON schema) or a cold table when ``WISP_COOCCUR_ONLINE`` is
+    set; ``None`` when neither is configured (fused_moe.py:596-631)."""
+    global _COOCCUR_TABLE
+    if _COOCCUR_TABLE is not None:
+        return _COOCCUR_TABLE or None
+    path = os.environ.get("WISP_COOCCUR_PATH", "").strip()
+    if not path and not _env_on("WISP_COOCCUR_ONLINE"):
+        return None
+    from .cooccur import CooccurTable
+    try:
+        _COOCCUR_TABLE = CooccurTable.load(path) if path and os.path.isfile(path) else CooccurTable()
+    except Exception as e:
+        logger.warning("wisp.vllm: cooccur table could not be loaded (%s); prefetch disabled", e)
+        _COOCCUR_TABLE = False
+        return None
+    return _COOCCUR_TABLE
+
+
+def _cooccur_predict_top_k(target_layer: int, k: int) -> list:
+    """Experts to prefetch into ``target_layer`` from this step's observations
+    at earlier layers (fused_moe.py:634-652: normalised, decay 0.5)."""
+    table = _COOCCUR_TABLE
+    if not table or not _CURRENT_STEP_OBS:
+        return []
+    from .cooccur import predict_layer
+    return predict_layer(table, _CURRENT_STEP_OBS, target_layer, k=k, normalize=True, decay=0.5,
+                         only_prev_layer=False)
+
+
+def _post_forward(state: WispMoEState, last_set: set) -> None:
+    """After a paged forward: record its unique experts for this step, predict
+    ``max(8, cap // 2)`` experts for the next layer and prefetch them; after
+    the last layer, learn the step online (fused_moe.py:1170-1233)."""
+    table = _maybe_load_cooccur() if _env_on("WISP_PREFETCH") else None
+    if table is None or not last_set:
+        return
+    _CURRENT_STEP_OBS[state.layer_idx] = last_set
+    nxt = state.layer_idx + 1
+    if nxt < len(_LAYER_STATES):
+        ns = _LAYER_STATES[nxt]
+        predicted = _cooccur_predict_top_k(nxt, max(8, ns.cap_experts // 2))
+        if predicted and ns.mode == _Mode.PAGED:
+            try:
+                ns.prefetch_async(set(predicted))
+                ns.stats_pred_total += len(predicted)
+            except Exception as e:
+                logger.debug("wisp.vllm: prefetch_async failed: %s", e)
+    if state.layer_idx == len(_LAYER_STATES) - 1:
+        if _env_on("WISP_COOCCUR_ONLINE"):
+            try:
+                table.observe_step(_CURRENT_STEP_OBS)
+            except Exception:
+                pass
+        _CURRENT_STEP_OBS.clear()
 
 
 def resize_layer_caps(new_cap: int) -> int:
@@ -499,6 +616,8 @@ def _patched_forward_cuda(self, layer: torch.nn.Module, x: torch.Tensor, topk_we
         return type(self)._wisp_original_forward_cuda(self, layer, x, topk_weights, topk_ids,
                                                       shared_experts, shared_experts_input)
     out = state.forward(x, topk_weights, topk_ids)
+    if state.mode == _Mode.PAGED and _env_on("WISP_PREFETCH"):
+        _post_forward(state, state.last_unique_experts)
     _apply_shared(shared_experts, shared_experts_input)
     return out
 
@@ -546,4 +665,4 @@ def is_installed(_cls=None) -> bool:
     return bool(getattr(cls, _PATCHED_FLAG, False))
 
 
-__all__ = ["install_wisp_moe", "is_installed", "WispMoEState"]
+__all__ = ["install_wisp_moe", "is_installed", "WispMoEState", "select_experts"]

@@ -73,11 +73,15 @@ def softmax_topk(logits: torch.Tensor, k: int, renormalize: bool = True):
     return w.contiguous(), ids.to(torch.int32).contiguous()
 
 
+def router_logits(T: int, E: int, seed: int = 0, zipf_s: float = 1.1) -> torch.Tensor:
+    """Config-1 router logits ``N(0,1) + zipf_bias`` (fp32, CPU)."""
+    g = torch.Generator().manual_seed(seed + 1)
+    return torch.randn(T, E, generator=g) + torch.from_numpy(zipf_bias(E, zipf_s, seed))
+
+
 def logits_routing(T: int, E: int, k: int, seed: int = 0, zipf_s: float = 1.1):
     """Config-1 routing: logits ``N(0,1) + zipf_bias`` -> softmax top-k."""
-    g = torch.Generator().manual_seed(seed + 1)
-    logits = torch.randn(T, E, generator=g) + torch.from_numpy(zipf_bias(E, zipf_s, seed))
-    return softmax_topk(logits, k)
+    return softmax_topk(router_logits(T, E, seed, zipf_s), k)
 
 
 def hidden_states(T: int, H: int, seed: int = 0) -> torch.Tensor:
