@@ -9,7 +9,8 @@
 // a fixed xor butterfly (16, 8, 4, 2, 1) combines the lanes -- a fixed order,
 // so p does not depend on anything but the row.  Top-k picks the k largest p
 // in descending order, ties to the lower expert id; renormalised weights are
-// w_j = p_j / (p_0 + ... + p_{k-1}), the sum taken in that order.
+// w_j = p_j / (p_0 + ... + p_{k-1}) with the sum and the quotient in double,
+// rounded once to fp32 (the correctly rounded renormalisation of the p_j).
 #include "common.cuh"
 
 namespace wisp {
@@ -67,7 +68,7 @@ __global__ void __launch_bounds__(kWarps * 32)
     // top-k: k rounds of a warp arg-max (largest p, then lowest id)
     float sel_p = 0.f;
     int sel_e = 0;
-    float tot = 0.f;
+    double tot = 0.0;
     for (int j = 0; j < k; ++j) {
         float bp = -2.f;
         int be = 0x7fffffff;
@@ -98,11 +99,11 @@ __global__ void __launch_bounds__(kWarps * 32)
             sel_p = bp;
             sel_e = be;
         }
-        tot += bp;  // every lane holds the same running sum, in selection order
+        tot += (double)bp;  // every lane holds the same running sum, in selection order
     }
     if (lane < k) {
         out_ids[(size_t)t * k + lane] = sel_e;
-        out_w[(size_t)t * k + lane] = renorm ? sel_p / tot : sel_p;
+        out_w[(size_t)t * k + lane] = renorm ? (float)((double)sel_p / tot) : sel_p;
     }
 }
 
