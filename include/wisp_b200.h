@@ -66,6 +66,22 @@ WISP_API int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t
 WISP_API int wisp_layer_destroy(wisp_layer *layer);
 
 /*
+ * Create a block-quantised FP8 layer: the reference's WispMoEStateFP8
+ * (fused_moe_fp8.py:61-145), which pages (weight, scale) pairs.  Host masters
+ * (pinned, caller-owned): w13 [E][2I][H] and w2 [E][H][I] float8_e4m3fn, and
+ * their per-128x128-block fp32 scales s13 [E][2I/128][H/128] and s2
+ * [E][H/128][I/128] (vLLM's w*_weight_scale_inv).  block_n = block_k = 128;
+ * hidden and inter multiples of 128.  Paging, the pager and every other entry
+ * point behave as for a bf16 layer; the compute is W8A8 with per-token-group
+ * activation quantisation (the arithmetic of vLLM's block-FP8 fused_experts)
+ * on the CUDA cores, through the host-synchronous forward at every call size.
+ */
+WISP_API int wisp_layer_create_fp8(int32_t num_experts, int32_t cap_experts, int32_t hidden, int32_t inter,
+                                   int32_t block_n, int32_t block_k, const void *host_w13, const void *host_w2,
+                                   const void *host_s13, const void *host_s2, int32_t device, int32_t mode,
+                                   wisp_layer **out);
+
+/*
  * Paged MoE forward of ``num_tokens`` rows, enqueued on ``stream`` (the call
  * returns before the work runs; see wisp_layer_sync for errors).  Replaces the pager + compute of
  * _wisp_forward_cuda_paged (fused_moe.py:1017, 1102-1168) and vLLM
@@ -147,6 +163,9 @@ WISP_API int wisp_set_stats(wisp_layer *layer, const int64_t *stats4);
 /* Device addresses of the slot scratch and expert map (for zero-copy views). */
 WISP_API int wisp_layer_buffers(wisp_layer *layer, void **scratch_w13, void **scratch_w2,
                        void **expert_map);
+
+/* Device addresses of an FP8 layer's slot scales (scratch_s13, scratch_s2). */
+WISP_API int wisp_layer_scale_buffers(wisp_layer *layer, void **scratch_s13, void **scratch_s2);
 
 /*
  * Cumulative telemetry (synchronises the device): {groups run, misses,

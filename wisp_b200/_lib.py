@@ -45,6 +45,9 @@ SIGNATURES = {
     "wisp_layer_create": (ctypes.c_int, [_c_int32, _c_int32, _c_int32, _c_int32, _c_int64, _c_int64,
                                          _vp, _vp, _c_int32, _c_int32, ctypes.POINTER(_vp)]),
     "wisp_layer_destroy": (ctypes.c_int, [_vp]),
+    "wisp_layer_create_fp8": (ctypes.c_int, [_c_int32, _c_int32, _c_int32, _c_int32, _c_int32, _c_int32,
+                                             _vp, _vp, _vp, _vp, _c_int32, _c_int32, ctypes.POINTER(_vp)]),
+    "wisp_layer_scale_buffers": (ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "wisp_moe_forward": (ctypes.c_int, [_vp, _vp, _pf, _vp, _c_int32, _c_int32, _c_int32, _vp, _vp]),
     "wisp_route_topk": (ctypes.c_int, [_vp, _c_int32, _c_int32, _c_int32, _c_int32, _c_int32, _vp, _vp, _vp]),
     "wisp_ensure_resident": (ctypes.c_int, [_vp, _vp, _c_int32, _c_int32, _vp]),

@@ -584,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 block_of(L, tl.b, u, q0, rows);
                 const int slot = L.slot[u];
                 const CUtensorMap *mw, *mt;
-                int a0, a1, kbc;
+                int a0, a1, kbc, kb0 = 0;
                 if (!tl.down) {
                     mw = &map_w13;
                     mt = &map_x;
@@ -596,11 +596,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     if (g.route && !gathered) {
-                        if (!wait_ready(g, kGatheredWord, gridDim.x, abort)) {
+                        // the weight boxes of the ring's unused stages go out now and
+                        // stream while the other CTAs finish gathering the token rows;
+                        // the token boxes follow the wait (issued even when the wait
+                        // gives up, so every stage's transaction completes)
+                        const int pre = max(0, min(kbc, kStages - kstep));
+                        for (int q = 0; q < pre; ++q) {
+                            const int s = kstep + q;
+                            unsigned char *st = stages + s * kStageBytes;
+                            mbar_expect_tx(&R.full[s], kStageBytes);
+                            tma_load_2d_hint(st, mw, q * kBK, a0, &R.full[s], once);
+                            tma_load_2d_hint(st + kWBoxBytes, mw, q * kBK, a1, &R.full[s], once);
+                        }
+                        if (pre > 0) trace_at(g.trace, kTrFirstLoad);
+                        const bool ok = wait_ready(g, kGatheredWord, gridDim.x, abort);
+                        for (int q = 0; q < pre; ++q) {
+                            const int s = kstep + q;
+                            tma_load_2d(stages + s * kStageBytes + 2 * kWBoxBytes, mt, q * kBK, q0, &R.full[s]);
+                        }
+                        kstep += pre;
+                        kb0 = pre;
+                        R.issued = kstep;
+                        gathered = true;
+                        if (!ok) {
                             give_up(R, g);
                             break;
                         }
-                        gathered = true;
                     }
                 } else {
                     mw = &map_w2;
@@ -614,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 bool ok = true;
-                for (int kb = 0; kb < kbc; ++kb, ++kstep) {
+                for (int kb = kb0; kb < kbc; ++kb, ++kstep) {
                     const int s = kstep % kStages;
                     if (kstep >= kStages &&
                         !mbar_wait(&R.empty[s], ((kstep / kStages) - 1) & 1, g.wait_ns, abort)) {

@@ -42,6 +42,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "forward.cuh"
+#include "fp8.cuh"
 #include "pager.cuh"
 #include "prefill.cuh"
 
@@ -117,6 +118,13 @@ struct wisp_layer {
     int64_t b13 = 0, b2 = 0;
     const char *h13 = nullptr, *h2 = nullptr;
     char *d13 = nullptr, *d2 = nullptr;
+    // block-quantised FP8 layers: per-expert fp32 block scales beside the weights
+    bool fp8 = false;
+    int64_t bs13 = 0, bs2 = 0;
+    const char *hs13 = nullptr, *hs2 = nullptr;
+    char *ds13 = nullptr, *ds2 = nullptr;
+    uint8_t *d_xq = nullptr, *d_aq = nullptr;  // FP8 workspace: quantised tokens and activations
+    float *d_xs = nullptr, *d_as = nullptr;
     int32_t *d_s2e = nullptr, *d_emap = nullptr;
     int64_t *d_tick = nullptr, *d_hdr = nullptr;
     uint32_t *d_slot_gen = nullptr, *d_slot_ready = nullptr;
@@ -176,6 +184,12 @@ int issue_pagein(wisp_layer *L, int64_t e, int64_t s, uint32_t gen) {
                                   cudaMemcpyHostToDevice, L->copy_stream));
     WISP_CUDA_TRY(cudaMemcpyAsync(L->d2 + s * L->b2, L->h2 + e * L->b2, L->b2, cudaMemcpyHostToDevice,
                                   L->copy_stream));
+    if (L->fp8) {  // the (weight, scale) pairs travel together
+        WISP_CUDA_TRY(cudaMemcpyAsync(L->ds13 + s * L->bs13, L->hs13 + e * L->bs13, L->bs13,
+                                      cudaMemcpyHostToDevice, L->copy_stream));
+        WISP_CUDA_TRY(cudaMemcpyAsync(L->ds2 + s * L->bs2, L->hs2 + e * L->bs2, L->bs2, cudaMemcpyHostToDevice,
+                                      L->copy_stream));
+    }
     if (g_write32) {
         CUresult r = g_write32(reinterpret_cast<CUstream>(L->copy_stream),
                                reinterpret_cast<CUdeviceptr>(L->d_slot_ready + s), gen, 0);
@@ -350,8 +364,11 @@ void free_ws(wisp_layer *L) {
                     (void *)L->d_grp_nhit, (void *)L->d_u_slot,
                     (void *)L->d_u_gen, (void *)L->d_u_off, (void *)L->d_u_pairs, (void *)L->d_counters,
                     (void *)L->d_dev_hdr, (void *)L->d_act, (void *)L->d_y, (void *)L->d_xperm,
-                    (void *)L->d_actperm, (void *)L->d_ready, (void *)L->d_combined})
+                    (void *)L->d_actperm, (void *)L->d_ready, (void *)L->d_combined, (void *)L->d_xq,
+                    (void *)L->d_aq, (void *)L->d_xs, (void *)L->d_as})
         cudaFree(p);
+    L->d_xq = L->d_aq = nullptr;
+    L->d_xs = L->d_as = nullptr;
     if (L->h_mb) cudaFreeHost(L->h_mb);
     L->d_slots = L->d_grp_start = L->d_grp_nu = L->d_grp_nhit = L->d_u_slot = L->d_u_gen = L->d_u_off =
         L->d_u_pairs = L->d_counters = L->d_dev_hdr = nullptr;
@@ -388,6 +405,12 @@ int ensure_ws(wisp_layer *L, int T, int K) {
     const int nblk = (H + 3) / 4;  // row quads (forward kernel) >= row octets (decode kernels)
     WISP_CUDA_TRY(cudaMalloc(&L->d_counters, sizeof(int32_t) * nblk));
     WISP_CUDA_TRY(cudaMemset(L->d_counters, 0, sizeof(int32_t) * nblk));
+    if (L->fp8) {
+        WISP_CUDA_TRY(cudaMalloc(&L->d_xq, (size_t)nT * H));
+        WISP_CUDA_TRY(cudaMalloc(&L->d_xs, sizeof(float) * (size_t)nT * (H / kFp8Block)));
+        WISP_CUDA_TRY(cudaMalloc(&L->d_aq, P * (size_t)I));
+        WISP_CUDA_TRY(cudaMalloc(&L->d_as, sizeof(float) * P * (I / kFp8Block)));
+    }
     if (L->H > 0 && L->I > 0) {
         // two halves, by launch parity (the one-launch forward polls its half)
         WISP_CUDA_TRY(cudaMalloc(&L->d_act, sizeof(__nv_bfloat16) * 2 * P * I));
@@ -427,6 +450,10 @@ int ensure_events(wisp_layer *L, int G) {
 int alloc_slots(wisp_layer *L, int cap) {
     WISP_CUDA_TRY(cudaMalloc(&L->d13, (size_t)cap * L->b13));
     WISP_CUDA_TRY(cudaMalloc(&L->d2, (size_t)cap * L->b2));
+    if (L->fp8) {
+        WISP_CUDA_TRY(cudaMalloc(&L->ds13, (size_t)cap * L->bs13));
+        WISP_CUDA_TRY(cudaMalloc(&L->ds2, (size_t)cap * L->bs2));
+    }
     WISP_CUDA_TRY(cudaMalloc(&L->d_s2e, sizeof(int32_t) * cap));
     WISP_CUDA_TRY(cudaMalloc(&L->d_tick, sizeof(int64_t) * cap));
     WISP_CUDA_TRY(cudaMalloc(&L->d_slot_gen, sizeof(uint32_t) * cap));
@@ -565,9 +592,10 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
 // Which kernels run a call's expert compute.  The choice depends on the
 // call's size (T * k) only, not on its grouping, so outputs stay
 // byte-identical across caps, modes and slot placements.
-enum class Path { kDecode, kBatchTC, kPrefillTC };
+enum class Path { kDecode, kBatchTC, kPrefillTC, kFp8 };
 Path compute_path(const wisp_layer *L, int T, int K) {
     const long pairs = (long)T * K;
+    if (L->fp8) return Path::kFp8;
     if (!prefill_shapes_supported(L->H, L->I) || L->compute_class == 1) return Path::kDecode;
     if (pairs >= kPrefillMinPairs) return Path::kPrefillTC;
     if (L->compute_class == 2) return Path::kBatchTC;
@@ -652,6 +680,12 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
     int rc = ensure_events(L, std::max(G, 1));
     if (rc) return rc;
     const Path path = compute_path(L, T, K);
+    if (compute && path == Path::kFp8 && T > 0) {
+        // the call's tokens, quantised once for every group
+        rc = launch_fp8_quant_rows(reinterpret_cast<const __nv_bfloat16 *>(x), T, L->H, L->d_xq, L->d_xs, stream);
+        if (rc) return rc;
+        ++L->launches;
+    }
     int mi = 0;
     for (int g = 0; g < G; ++g) {
         const int t0 = grp[g], t1 = grp[g + 1];
@@ -673,12 +707,42 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
             WISP_CUDA_TRY(cudaEventRecord(L->ev_copy[g], L->copy_stream));
             if (!slot_waits) WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copy[g], 0));
         }
-        if (compute && t1 > t0 && nu[g] > 0 && path != Path::kDecode) {
+        const bool tensor_cores = path == Path::kBatchTC || path == Path::kPrefillTC;
+        if (compute && t1 > t0 && nu[g] > 0 && tensor_cores) {
             // tensor-core kernels (gather, gate-up + SiLU-mul, down, combine)
             PrefillGroup pg = tc_group(L, x, w, out, g, t0, t1, K, nu[g], nullptr);
             if (slot_waits && mi > m0) pg.u_gen = L->d_u_gen + (int64_t)t0 * K;
             rc = launch_tc_group(L, path, pg, stream);
             if (rc) return rc;
+        } else if (compute && t1 > t0 && nu[g] > 0 && path == Path::kFp8) {
+            const int64_t p0 = (int64_t)t0 * K;
+            Fp8Group fg{};
+            fg.xq = L->d_xq;
+            fg.xs = L->d_xs;
+            fg.w13 = reinterpret_cast<const uint8_t *>(L->d13);
+            fg.s13 = reinterpret_cast<const float *>(L->ds13);
+            fg.w2 = reinterpret_cast<const uint8_t *>(L->d2);
+            fg.s2 = reinterpret_cast<const float *>(L->ds2);
+            fg.u_slot = L->d_u_slot + p0;
+            fg.u_off = L->d_u_off + p0 + g;
+            fg.u_pairs = L->d_u_pairs + p0;
+            fg.nu = L->d_grp_nu + g;
+            fg.topk_w = w;
+            fg.act = L->d_act;
+            fg.aq = L->d_aq;
+            fg.as = L->d_as;
+            fg.y = L->d_y;
+            fg.out = reinterpret_cast<__nv_bfloat16 *>(out);
+            fg.counters = L->d_counters;
+            fg.K = K;
+            fg.H = L->H;
+            fg.I = L->I;
+            fg.t0 = t0;
+            fg.t1 = t1;
+            rc = launch_fp8_group(fg, nu[g], stream);
+            if (rc) return rc;
+            L->launches += kFp8KernelsPerGroup;
+            L->act_dirty = true;
         } else if (compute && t1 > t0 && nu[g] > 0) {
             const int64_t p0 = (int64_t)t0 * K;
             GroupCompute gc{};
@@ -833,15 +897,11 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
 
 }  // namespace
 
-extern "C" {
-
-const char *wisp_version(void) { return "wisp_b200 0.2.0 (sm_100a)"; }
-
-const char *wisp_last_error(void) { return g_last_error.c_str(); }
-
-int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, int32_t inter,
-                      int64_t w13_expert_bytes, int64_t w2_expert_bytes, const void *host_w13,
-                      const void *host_w2, int32_t device, int32_t mode, wisp_layer **out) {
+static int layer_create_impl(int32_t num_experts, int32_t cap_experts, int32_t hidden, int32_t inter,
+                             int64_t w13_expert_bytes, int64_t w2_expert_bytes, const void *host_w13,
+                             const void *host_w2, int32_t device, int32_t mode, wisp_layer **out,
+                             const void *host_s13 = nullptr, const void *host_s2 = nullptr) {
+    const bool fp8 = host_s13 != nullptr;
     if (!out) return fail(WISP_ERR_INVALID, "wisp_layer_create: out is NULL");
     *out = nullptr;
     if (num_experts < 1 || num_experts > 1024)
@@ -855,7 +915,7 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     if (w13_expert_bytes <= 0 || w2_expert_bytes <= 0 || !host_w13 || !host_w2)
         return fail(WISP_ERR_INVALID, "wisp_layer_create: empty expert weights");
     if (hidden < 0 || inter < 0) return fail(WISP_ERR_INVALID, "wisp_layer_create: negative shape");
-    if (hidden > 0 && inter > 0) {
+    if (hidden > 0 && inter > 0 && !fp8) {
         if (hidden % 8 || inter % 8)
             return fail(WISP_ERR_UNSUPPORTED, "wisp_layer_create: hidden and inter must be multiples of 8");
         if (w13_expert_bytes != 2LL * 2 * inter * hidden || w2_expert_bytes != 2LL * hidden * inter)
@@ -869,7 +929,7 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     // allocations below (see ensure_ws)
     WISP_CUDA_TRY(cudaDeviceSynchronize());
     cudaPointerAttributes pa{};
-    for (const void *hp : {host_w13, host_w2}) {
+    for (const void *hp : {host_w13, host_w2, fp8 ? host_s13 : host_w13, fp8 ? host_s2 : host_w2}) {
         if (cudaPointerGetAttributes(&pa, hp) != cudaSuccess || pa.type != cudaMemoryTypeHost) {
             cudaGetLastError();
             return fail(WISP_ERR_INVALID, "wisp_layer_create: host expert weights must be pinned");
@@ -886,6 +946,13 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     L->b2 = w2_expert_bytes;
     L->h13 = reinterpret_cast<const char *>(host_w13);
     L->h2 = reinterpret_cast<const char *>(host_w2);
+    if (fp8) {
+        L->fp8 = true;
+        L->bs13 = sizeof(float) * (2LL * inter / kFp8Block) * (hidden / kFp8Block);
+        L->bs2 = sizeof(float) * (1LL * hidden / kFp8Block) * (inter / kFp8Block);
+        L->hs13 = reinterpret_cast<const char *>(host_s13);
+        L->hs2 = reinterpret_cast<const char *>(host_s2);
+    }
     auto bail = [&](int rc) {
         wisp_layer_destroy(L);
         return rc;
@@ -931,7 +998,7 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     // kernel -- the kernel then waits until its limit.  WISP_CFG_ASYNC = 1
     // opts a paged layer in where the caller queues nothing on the device
     // while its forwards page in.
-    L->async = (mode == WISP_MODE_RESIDENT);
+    L->async = (mode == WISP_MODE_RESIDENT) && !fp8;
     {
         int sms = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 0;
@@ -943,13 +1010,43 @@ int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, 
     return WISP_OK;
 }
 
+
+extern "C" {
+
+const char *wisp_version(void) { return "wisp_b200 0.2.0 (sm_100a)"; }
+
+const char *wisp_last_error(void) { return g_last_error.c_str(); }
+
+int wisp_layer_create(int32_t num_experts, int32_t cap_experts, int32_t hidden, int32_t inter,
+                      int64_t w13_expert_bytes, int64_t w2_expert_bytes, const void *host_w13,
+                      const void *host_w2, int32_t device, int32_t mode, wisp_layer **out) {
+    return layer_create_impl(num_experts, cap_experts, hidden, inter, w13_expert_bytes, w2_expert_bytes,
+                             host_w13, host_w2, device, mode, out);
+}
+
+int wisp_layer_create_fp8(int32_t num_experts, int32_t cap_experts, int32_t hidden, int32_t inter,
+                          int32_t block_n, int32_t block_k, const void *host_w13, const void *host_w2,
+                          const void *host_s13, const void *host_s2, int32_t device, int32_t mode,
+                          wisp_layer **out) {
+    if (!out) return fail(WISP_ERR_INVALID, "wisp_layer_create_fp8: out is NULL");
+    *out = nullptr;
+    if (block_n != kFp8Block || block_k != kFp8Block)
+        return fail(WISP_ERR_UNSUPPORTED, "wisp_layer_create_fp8: weight blocks must be 128 x 128");
+    if (hidden <= 0 || inter <= 0 || hidden % kFp8Block || inter % kFp8Block)
+        return fail(WISP_ERR_UNSUPPORTED, "wisp_layer_create_fp8: hidden and inter must be multiples of 128");
+    if (!host_s13 || !host_s2) return fail(WISP_ERR_INVALID, "wisp_layer_create_fp8: NULL scales");
+    return layer_create_impl(num_experts, cap_experts, hidden, inter, 2LL * inter * hidden, 1LL * hidden * inter,
+                             host_w13, host_w2, device, mode, out, host_s13, host_s2);
+}
+
 int wisp_layer_destroy(wisp_layer *L) {
     if (!L) return WISP_OK;
     DeviceGuard guard(L->dev);
     if (L->ev_last) drain(L);
     cudaDeviceSynchronize();
     free_ws(L);
-    for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->d_s2e, (void *)L->d_tick, (void *)L->d_emap,
+    for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->ds13, (void *)L->ds2, (void *)L->d_s2e,
+                    (void *)L->d_tick, (void *)L->d_emap,
                     (void *)L->d_hdr, (void *)L->d_slot_gen, (void *)L->d_slot_ready, (void *)L->d_bar,
                     (void *)L->d_flow, (void *)L->d_last_unique})
         cudaFree(p);
@@ -988,7 +1085,13 @@ int wisp_moe_forward(wisp_layer *L, const void *x, const float *topk_weights,
     if (rc) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const Path path = compute_path(L, num_tokens, top_k);
-    if (L->async && num_tokens > 0 && path != Path::kDecode && L->mode == WISP_MODE_RESIDENT)
+    if (path == Path::kFp8) {  // FP8 layers: the host-synchronous path, every call size
+        rc = run_pager(L, topk_ids, ids_int64, num_tokens, top_k, 0, 1, s);
+        if (rc) return rc;
+        return page_and_compute(L, x, topk_weights, num_tokens, top_k, out, s, true);
+    }
+    if (L->async && num_tokens > 0 && (path == Path::kBatchTC || path == Path::kPrefillTC) &&
+        L->mode == WISP_MODE_RESIDENT)
         return forward_tc_resident(L, path, x, topk_weights, topk_ids, ids_int64, num_tokens, top_k, out, s);
     if (L->async && top_k <= L->cap && path == Path::kDecode)
         return forward_async(L, x, topk_weights, topk_ids, ids_int64, num_tokens, top_k, out, s);
@@ -1101,6 +1204,12 @@ int wisp_prime_identity(wisp_layer *L, void *stream) {
                                   L->copy_stream));
     WISP_CUDA_TRY(cudaMemcpyAsync(L->d2, L->h2, (size_t)L->E * L->b2, cudaMemcpyHostToDevice,
                                   L->copy_stream));
+    if (L->fp8) {
+        WISP_CUDA_TRY(cudaMemcpyAsync(L->ds13, L->hs13, (size_t)L->E * L->bs13, cudaMemcpyHostToDevice,
+                                      L->copy_stream));
+        WISP_CUDA_TRY(cudaMemcpyAsync(L->ds2, L->hs2, (size_t)L->E * L->bs2, cudaMemcpyHostToDevice,
+                                      L->copy_stream));
+    }
     WISP_CUDA_TRY(cudaMemcpy(L->d_s2e, ident.data(), sizeof(int32_t) * L->E, cudaMemcpyHostToDevice));
     WISP_CUDA_TRY(cudaMemcpy(L->d_emap, ident.data(), sizeof(int32_t) * L->E, cudaMemcpyHostToDevice));
     WISP_CUDA_TRY(cudaMemcpy(L->d_slot_ready, L->d_slot_gen, sizeof(uint32_t) * L->cap,
@@ -1130,17 +1239,19 @@ int wisp_resize_cap(wisp_layer *L, int32_t new_cap, void *stream) {
     WISP_CUDA_TRY(cudaMemcpy(tick.data(), L->d_tick, sizeof(int64_t) * old, cudaMemcpyDeviceToHost));
     WISP_CUDA_TRY(cudaMemcpy(emap.data(), L->d_emap, sizeof(int32_t) * L->E, cudaMemcpyDeviceToHost));
     WISP_CUDA_TRY(cudaMemcpy(gen.data(), L->d_slot_gen, sizeof(uint32_t) * old, cudaMemcpyDeviceToHost));
-    char *o13 = L->d13, *o2 = L->d2;
+    char *o13 = L->d13, *o2 = L->d2, *os13 = L->ds13, *os2 = L->ds2;
     int32_t *os2e = L->d_s2e;
     int64_t *otick = L->d_tick;
     uint32_t *ogen = L->d_slot_gen, *oready = L->d_slot_ready;
-    L->d13 = L->d2 = nullptr;
+    L->d13 = L->d2 = L->ds13 = L->ds2 = nullptr;
     if (alloc_slots(L, new_cap)) {
-        for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->d_s2e, (void *)L->d_tick,
-                        (void *)L->d_slot_gen, (void *)L->d_slot_ready})
+        for (void *p : {(void *)L->d13, (void *)L->d2, (void *)L->ds13, (void *)L->ds2, (void *)L->d_s2e,
+                        (void *)L->d_tick, (void *)L->d_slot_gen, (void *)L->d_slot_ready})
             cudaFree(p);
         L->d13 = o13;
         L->d2 = o2;
+        L->ds13 = os13;
+        L->ds2 = os2;
         L->d_s2e = os2e;
         L->d_tick = otick;
         L->d_slot_gen = ogen;
@@ -1149,6 +1260,10 @@ int wisp_resize_cap(wisp_layer *L, int32_t new_cap, void *stream) {
     }
     WISP_CUDA_TRY(cudaMemcpy(L->d13, o13, (size_t)keep * L->b13, cudaMemcpyDeviceToDevice));
     WISP_CUDA_TRY(cudaMemcpy(L->d2, o2, (size_t)keep * L->b2, cudaMemcpyDeviceToDevice));
+    if (L->fp8) {
+        WISP_CUDA_TRY(cudaMemcpy(L->ds13, os13, (size_t)keep * L->bs13, cudaMemcpyDeviceToDevice));
+        WISP_CUDA_TRY(cudaMemcpy(L->ds2, os2, (size_t)keep * L->bs2, cudaMemcpyDeviceToDevice));
+    }
     if (new_cap < old)
         for (int s = new_cap; s < old; ++s)
             if (s2e[s] >= 0) emap[s2e[s]] = -1;
@@ -1161,8 +1276,9 @@ int wisp_resize_cap(wisp_layer *L, int32_t new_cap, void *stream) {
     // every copy has landed at this barrier: generation flags equal the generations
     WISP_CUDA_TRY(cudaMemcpy(L->d_slot_gen, gen.data(), sizeof(uint32_t) * new_cap, cudaMemcpyHostToDevice));
     WISP_CUDA_TRY(cudaMemcpy(L->d_slot_ready, gen.data(), sizeof(uint32_t) * new_cap, cudaMemcpyHostToDevice));
-    for (void *p : {(void *)o13, (void *)o2, (void *)os2e, (void *)otick, (void *)ogen, (void *)oready})
-        cudaFree(p);
+    for (void *p : {(void *)o13, (void *)o2, (void *)os13, (void *)os2, (void *)os2e, (void *)otick, (void *)ogen,
+                    (void *)oready})
+        if (p) cudaFree(p);
     L->cap = new_cap;
     return WISP_OK;
 }
@@ -1202,6 +1318,14 @@ int wisp_layer_buffers(wisp_layer *L, void **scratch_w13, void **scratch_w2, voi
     if (scratch_w13) *scratch_w13 = L->d13;
     if (scratch_w2) *scratch_w2 = L->d2;
     if (expert_map) *expert_map = L->d_emap;
+    return WISP_OK;
+}
+
+int wisp_layer_scale_buffers(wisp_layer *L, void **scratch_s13, void **scratch_s2) {
+    if (!L) return fail(WISP_ERR_INVALID, "wisp_layer_scale_buffers: NULL layer");
+    if (!L->fp8) return fail(WISP_ERR_INVALID, "wisp_layer_scale_buffers: not an FP8 layer");
+    if (scratch_s13) *scratch_s13 = L->ds13;
+    if (scratch_s2) *scratch_s2 = L->ds2;
     return WISP_OK;
 }
 

@@ -10,5 +10,7 @@ Same entry points as the reference's ``wisp.integrations.vllm``
 and expert compute run in this package's sm_100a kernels.
 """
 from .fused_moe import WispMoEState, install_wisp_moe, is_installed
+from .fused_moe_fp8 import WispMoEStateFP8, install_wisp_fp8, is_fp8_installed
 
-__all__ = ["install_wisp_moe", "is_installed", "WispMoEState"]
+__all__ = ["install_wisp_moe", "is_installed", "WispMoEState", "install_wisp_fp8", "is_fp8_installed",
+           "WispMoEStateFP8"]

@@ -126,17 +126,19 @@ class WispMoEState:
             hidden, inter = int(self.cpu_w2.shape[1]), int(self.cpu_w2.shape[2])
         self.hidden_size, self.intermediate_size = hidden, inter
         cmode = _lib.MODE_RESIDENT if mode == _Mode.RESIDENT else _lib.MODE_PAGED
-        handle = ctypes.c_void_p()
-        _lib.check(_lib.lib().wisp_layer_create(
-            E, int(cap_experts), hidden, inter, b13, b2, self.cpu_w13.data_ptr(),
-            self.cpu_w2.data_ptr(), self.device.index, cmode, ctypes.byref(handle)),
-            "wisp_layer_create")
-        self._h = handle
+        self._h = self._create_native(E, int(cap_experts), hidden, inter, b13, b2, cmode)
         self._b13, self._b2 = b13, b2
         self.tc_min_pairs = self._query(_lib.CFG_TC_MIN_PAIRS)
         self.stats_pred_hits = 0
         self.stats_pred_total = 0
         self._refresh_views()
+
+    def _create_native(self, E, cap, hidden, inter, b13, b2, cmode):
+        handle = ctypes.c_void_p()
+        _lib.check(_lib.lib().wisp_layer_create(
+            E, cap, hidden, inter, b13, b2, self.cpu_w13.data_ptr(), self.cpu_w2.data_ptr(),
+            self.device.index, cmode, ctypes.byref(handle)), "wisp_layer_create")
+        return handle
 
     # ---- lifetime ---------------------------------------------------------
     def close(self) -> None:
@@ -654,6 +656,13 @@ def install_wisp_moe(*, mode: str | None = None, cap_experts: int | None = None,
     setattr(cls, _PATCHED_FLAG, True)
     logger.info("wisp.vllm: patched %s (mode=%s cap_experts=%s)", cls.__name__,
                 _WISP_RUNTIME_CONFIG["mode"], cap_experts)
+    if _cls is None:
+        # the block-quantised FP8 MoE path too, best effort (fused_moe.py:1297-1303)
+        try:
+            from .fused_moe_fp8 import install_wisp_fp8
+            install_wisp_fp8()
+        except Exception as e:
+            logger.warning("wisp.vllm: FP8 MoE patch not applied (%s)", e)
     return True
 
 
