@@ -428,6 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char *stages = align1024(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = g.H, I = g.I;
+    pdl_wait();
+    pdl_launch_dependents();
     if (threadIdx.x == 0) trace_at(g.trace, kTrEntry);
 
     // the next launch's counters
@@ -791,18 +793,8 @@ int launch_kernel(const PrefillGroup &p, const Args &a, long nu_bound, cudaStrea
     WISP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const long blocks = std::min<long>(nu_bound, p.npairs) + (p.npairs + kTN - 1) / kTN;
     const long tiles = blocks * (p.I / kWM + p.H / kDownRows);
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)std::max<long>(1, std::min<long>(tiles, sms)));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    WISP_CUDA_TRY(cudaLaunchKernelEx(&cfg, batch_moe_kernel, mw13, mw2, mx, mact, a));
-    return WISP_OK;
+    return launch_persistent(batch_moe_kernel, dim3((unsigned)std::max<long>(1, std::min<long>(tiles, sms))),
+                             dim3(kThreads), (size_t)kSmemBytes, stream, mw13, mw2, mx, mact, a);
 }
 
 int check_group(const PrefillGroup &p, const BatchCounters &c) {

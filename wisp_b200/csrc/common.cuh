@@ -27,6 +27,41 @@ void set_error(const std::string &msg);
         }                                                                            \
     } while (0)
 
+// Cooperative launch of a persistent kernel (every block resident: blocks wait
+// on one another), with programmatic dependent launch unless WISP_NO_PDL is
+// set: the launch may begin while the previous kernel on the stream drains,
+// and the kernel's pdl_wait() orders it after that kernel.  If the driver
+// refuses the two attributes together, the plain cooperative launch is used
+// from then on for that device.
+bool pdl_enabled(int dev);
+void pdl_refused(int dev);
+template <typename... KArgs, typename... Args>
+int launch_persistent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      Args... args) {
+    int dev = 0;
+    WISP_CUDA_TRY(cudaGetDevice(&dev));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    if (pdl_enabled(dev)) {
+        cfg.numAttrs = 2;
+        if (cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess) return WISP_OK;
+        (void)cudaGetLastError();  // a refused launch configuration, not a device fault
+        pdl_refused(dev);
+    }
+    cfg.numAttrs = 1;
+    WISP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+    return WISP_OK;
+}
+
 // ---- bf16 helpers -------------------------------------------------------
 __device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
@@ -119,6 +154,18 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while the kernel before it on the
+// stream still runs; pdl_wait() returns once that kernel has completed and
+// its memory is visible, so every read or write of device memory that other
+// work produced or consumes comes after it.  pdl_launch_dependents() lets the
+// next such kernel start (its blocks then occupy SMs this kernel's blocks
+// have left and wait there).  Both are no-ops for a plain launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Butterfly sum over the warp; every lane ends with the same value and the

@@ -117,6 +117,7 @@ struct Meta {
     int total;  // speculation lists: unique experts of the call (resident or not)
     int slot[kMetaU], gen[kMetaU], off[kMetaU + 1];
     int pair[kMetaP], tok[kMetaP];
+    float wt[kMetaP];  // routing weight of each list entry's pair
 };
 
 // ---- TMA-fed units (decode sizes) --------------------------------------------
@@ -399,7 +400,7 @@ __device__ __forceinline__ void dn_pass(const GroupCompute &a, const Meta &m, in
 #pragma unroll
     for (int t = 0; t < P; ++t) {
         const int p = m.pair[qb + t];
-        const float wp = a.topk_w[p];
+        const float wp = m.wt[qb + t];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const float sum = warp_sum(acc[r][t]);
@@ -617,13 +618,21 @@ __device__ bool run_stream(const GroupCompute &a, const Meta &m, const Stream &S
     return true;
 }
 
-// Row-quad arrivals of a warp's down units (after their y stores): one fence,
-// then one lane per unit; the last of the nu arrivals on a quad sums the
-// group's tokens over k in routing order for its rows.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Row-quad arrivals of a warp's down units (after their y stores): one lane
+// per unit counts itself in with an acquire-release atomic at GPU scope (after
+// a warp barrier, so the other lanes' y stores are released too); the units
+// that complete their quad (the nu-th arrival) then sum the group's tokens
+// over k in routing order for those rows, all of them in one pass over the
+// warp's lanes (one output per lane, its K loads in flight together).
 __device__ void arrive_stream(const GroupCompute &a, const Stream &S, int nu, int lane) {
     if (S.n_dn == 0 || S.j0 >= S.nch) return;
-    __threadfence();
-    __syncwarp();
+    const int per = (a.t1 - a.t0) * 4;  // outputs of one row quad
     // this warp's down units, 32 at a time (lane l takes the l-th)
     int j = S.j0, d = j * kDownChunk;
     while (j < S.nch) {
@@ -635,20 +644,28 @@ __device__ void arrive_stream(const GroupCompute &a, const Stream &S, int nu, in
                 d = j * kDownChunk;
             }
         }
+        __syncwarp();
         int last = 0, q = 0;
         if (mine >= 0) {
             q = mine % S.nq;
-            last = (atomicAdd(&a.counters[q], 1) == nu - 1);
+            last = atom_add_acq_rel_gpu(&a.counters[q], 1) == nu - 1;
         }
-        unsigned todo = __ballot_sync(0xffffffffu, last);
-        if (todo) __threadfence();
-        while (todo) {
-            const int l = __ffs(todo) - 1;
-            todo &= todo - 1;
-            const int ql = __shfl_sync(0xffffffffu, q, l);
-            combine_rows(a, ql * 4, 4, lane, 32);
-            if (lane == 0) a.counters[ql] = 0;
+        const unsigned todo = __ballot_sync(0xffffffffu, last);
+        __syncwarp();
+        const int n = __popc(todo) * per;
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            const int idx = i0 + lane;
+            const int which = idx < n ? idx / per : 0;
+            unsigned m = todo;
+            for (int i = 0; i < which; ++i) m &= m - 1;
+            const int qv = __shfl_sync(0xffffffffu, q, m ? __ffs(m) - 1 : 0);
+            if (idx < n) {
+                const int rem = idx - which * per;
+                const int hh = qv * 4 + (rem & 3);
+                if (hh < a.H) combine_one(a, a.t0 + (rem >> 2), hh);
+            }
         }
+        if (last) a.counters[q] = 0;
     }
 }
 
@@ -708,12 +725,16 @@ __device__ bool build_spec_meta(const ForwardParams &fp, Meta &m, int *pos) {
     const int P = pg.T * pg.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (P > kSpecMaxPairs || pg.E > 1024) return false;
     int *s_emap = pos + pg.E;
+    // this thread's routed id (P <= kSpecMaxPairs <= blockDim.x) in flight
+    // together with the map: one global round trip
+    const long long my_e = tid < P ? load_id64(pg.ids, pg.ids64, tid) : 0;
+    const float my_w = tid < P ? fp.gc.topk_w[tid] : 0.f;
     if (tid < 32) s_mask[tid] = 0;
     if (tid == 0) s_flag = 0;
     for (int e = tid; e < pg.E; e += blockDim.x) s_emap[e] = pg.emap[e];
     __syncthreads();
     for (int p = tid; p < P; p += blockDim.x) {
-        const long long e = load_id64(pg.ids, pg.ids64, p);
+        const long long e = my_e;
         if (e < 0 || e >= pg.E) {
             s_flag = 1;
         } else {
@@ -787,6 +808,7 @@ __device__ bool build_spec_meta(const ForwardParams &fp, Meta &m, int *pos) {
     if (at >= 0) {
         m.pair[at] = p;
         m.tok[at] = p / pg.K;
+        m.wt[at] = my_w;
     }
     __syncthreads();
     return true;
@@ -806,6 +828,7 @@ __device__ bool load_meta(const ForwardParams &fp, int g, long p0, int nu, int n
         const int p = __ldcg(pg.u_pairs + p0 + i);
         m.pair[i] = p;
         m.tok[i] = p / pg.K;
+        m.wt[i] = fp.gc.topk_w[p];
     }
     __syncthreads();
     if (tid == 0) {
@@ -873,11 +896,10 @@ __global__ void __launch_bounds__(NW * 32, kBlocksPerSm) forward_kernel(const __
     do {                                                                                 \
         if (tr && tid == 0 && blockIdx.x == 0) tr[(slot)] = globaltimer_ns();            \
     } while (0)
+    pdl_wait();
+    pdl_launch_dependents();
     WISP_TRACE(0);
     WISP_TRACE0(0);
-    // the next launch's activation buffer: every element "not written yet"
-    for (long i = (long)blockIdx.x * (NW * 32) + tid; i < a.act_reset_words; i += (long)gridDim.x * (NW * 32))
-        a.act_reset[i] = 0xFFFFFFFFu;
 
     // per-warp copy pipelines (FAST variant); buffers overlay the pager's shared
     // memory, which block 0 is done with before its first copy
@@ -1025,6 +1047,11 @@ __global__ void __launch_bounds__(NW * 32, kBlocksPerSm) forward_kernel(const __
         }
     }
 done:
+    // the next launch's activation buffer: every element "not written yet"
+    // (after this launch's work, so these stores do not hold up its fences;
+    // every block gets here, aborts included)
+    for (long i = (long)blockIdx.x * (NW * 32) + tid; i < a.act_reset_words; i += (long)gridDim.x * (NW * 32))
+        a.act_reset[i] = 0xFFFFFFFFu;
     WISP_TRACE0(4);
 #undef WISP_TRACE
 #undef WISP_TRACE0
@@ -1056,11 +1083,7 @@ int launch_t(const ForwardParams &p, size_t smem, cudaStream_t stream) {
     int sms = 0;
     WISP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     dim3 grid(sms * nblk_per_sm[dev]), block(NW * 32);
-    ForwardParams arg = p;
-    void *args[] = {&arg};
-    WISP_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)forward_kernel<MAXP, FAST, NW>, grid, block, args,
-                                              smem, stream));
-    return WISP_OK;
+    return launch_persistent(forward_kernel<MAXP, FAST, NW>, grid, block, smem, stream, p);
 }
 
 }  // namespace

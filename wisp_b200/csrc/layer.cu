@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <chrono>
 #include <condition_variable>
 #include <deque>
@@ -50,6 +51,18 @@ namespace wisp {
 
 static thread_local std::string g_last_error;
 void set_error(const std::string &msg) { g_last_error = msg; }
+
+namespace {
+std::atomic<int> g_pdl_state[64];  // 0 untried / accepted, 1 refused
+int pdl_env() {
+    static const int v = std::getenv("WISP_NO_PDL") ? 0 : 1;
+    return v;
+}
+}  // namespace
+bool pdl_enabled(int dev) { return pdl_env() && dev >= 0 && dev < 64 && g_pdl_state[dev].load() == 0; }
+void pdl_refused(int dev) {
+    if (dev >= 0 && dev < 64) g_pdl_state[dev].store(1);
+}
 
 namespace {
 

@@ -190,18 +190,32 @@ __device__ __forceinline__ void down_quad(const GroupCompute &a, int u, int h0, 
     }
 }
 
+// out[t][hh] = the routing-order sum (combine_add) of the bf16 rows
+// y[t K + k][hh], k = 0 .. K-1, rounded to bf16; up to 8 of the loads are in
+// flight at once (L2, past L1: the rows come from other blocks).
+__device__ __forceinline__ void combine_one(const GroupCompute &a, int t, int hh) {
+    const int H = a.H, K = a.K;
+    const unsigned short *col = reinterpret_cast<const unsigned short *>(a.y) + (size_t)t * K * H + hh;
+    float acc = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 8) {
+        unsigned short v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (k0 + j < K) v[j] = __ldcg(col + (size_t)(k0 + j) * H);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (k0 + j < K) acc = combine_add(acc, bf16lo((uint32_t)v[j]), K);
+    }
+    a.out[(size_t)t * H + hh] = __float2bfloat16_rn(acc);
+}
+
 // out rows [h0, h0 + rows) of the group's tokens: sum over k in routing order.
 __device__ __forceinline__ void combine_rows(const GroupCompute &a, int h0, int rows, int tid,
                                              int nthreads) {
-    const int ntok = a.t1 - a.t0, H = a.H, K = a.K;
+    const int ntok = a.t1 - a.t0, H = a.H;
     for (int idx = tid; idx < ntok * rows; idx += nthreads) {
-        const int t = a.t0 + idx / rows;
         const int hh = h0 + idx % rows;
-        if (hh >= H) continue;
-        float acc = 0.f;
-        for (int k = 0; k < K; ++k)
-            acc = combine_add(acc, __bfloat162float(__ldcg(a.y + ((size_t)t * K + k) * H + hh)), K);
-        a.out[(size_t)t * H + hh] = __float2bfloat16_rn(acc);
+        if (hh < H) combine_one(a, a.t0 + idx / rows, hh);
     }
 }
 
