@@ -77,3 +77,36 @@ def test_prefill_pager_state_and_kernel_count():
         assert s2e == oracle.slot_to_expert and tick == oracle.lru_tick and clock == oracle.lru_clock
         assert stats == oracle.stats()
     st.close()
+
+
+def test_resident_prefill_routes_on_the_device():
+    """A resident call of prefill size: one routing kernel writes the group
+    lists (pairs sorted by expert) and counts only the
+    forward, as the reference's resident mode does (no LRU bookkeeping: a
+    resident layer pages nothing); then gather, both GEMMs and combine.  A
+    routed id outside [0, E) fails the call with WISP_ERR_BAD_EXPERT before
+    any counter changes and leaves the output alone; the layer keeps working."""
+    from wisp_b200 import _lib
+    E, H, I, T, K = 32, 256, 128, 300, 4
+    w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=31)
+    st = state(w13, w2, E, "resident")
+    l0 = st.telemetry()["kernel_launches"]
+    out = fwd(st, x, w, ids)
+    assert st.telemetry()["kernel_launches"] - l0 == 5
+    s2e, tick, clock, stats = st._read()
+    assert s2e == list(range(E)) and stats == [1, 0, 0, 0]
+    assert st.telemetry()["unique_experts"] == len(set(ids.reshape(-1).tolist()))
+    c = compare(out, moe_reference(x, w13, w2, w, ids))
+    assert c["mean_rel"] <= MEAN_REL, c
+    bad = ids.clone()
+    bad[T // 2, 1] = E
+    sentinel = torch.full((T, H), 3.0, dtype=torch.bfloat16, device=DEV)
+    st.forward(x.to(DEV), w.to(DEV), bad.to(DEV), out=sentinel)
+    with pytest.raises(_lib.WispError) as ei:
+        st.synchronize()
+    assert ei.value.code == _lib.WISP_ERR_BAD_EXPERT
+    assert bool((sentinel == 3.0).all())
+    assert st._read()[3] == [1, 0, 0, 0]
+    assert torch.equal(fwd(st, x, w, ids), out)
+    assert st._read()[3] == [2, 0, 0, 0]
+    st.close()

@@ -62,6 +62,33 @@ int launch_persistent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
     return WISP_OK;
 }
 
+// The same for a kernel whose blocks do not wait on one another (no
+// cooperative launch), still with programmatic dependent launch.
+template <typename... KArgs, typename... Args>
+int launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args... args) {
+    int dev = 0;
+    WISP_CUDA_TRY(cudaGetDevice(&dev));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    if (pdl_enabled(dev)) {
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess) return WISP_OK;
+        (void)cudaGetLastError();
+        pdl_refused(dev);
+    }
+    cfg.numAttrs = 0;
+    WISP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+    return WISP_OK;
+}
+
 // ---- bf16 helpers -------------------------------------------------------
 __device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }

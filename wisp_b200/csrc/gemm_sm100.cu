@@ -1,6 +1,7 @@
 // Prefill expert compute for one token group on tcgen05 tensor cores; see
 // gemm_sm100.cuh for the data flow and the kernel structure.
 #include "gemm_sm100.cuh"
+#include "pager.cuh"
 #include "prefill.cuh"
 
 #include <algorithm>
@@ -21,6 +22,8 @@ __device__ __forceinline__ unsigned char *align1024(unsigned char *p) {
 // sticky word.
 __global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int K, int H8, uint4 *xp,
                               const int32_t *pager_status, int *status) {
+    pdl_wait();
+    pdl_launch_dependents();
     if (pager_status) {
         const int st = *reinterpret_cast<const volatile int32_t *>(pager_status);
         if (st != WISP_OK) {
@@ -33,6 +36,123 @@ __global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int
     const uint4 *src = x + (size_t)(u_pairs[q] / K) * H8;
     uint4 *dst = xp + (size_t)q * H8;
     for (int c = threadIdx.x & 31; c < H8; c += 32) dst[c] = src[c];
+}
+
+// ---- routing of a resident call (one block) --------------------------------------
+// Counting sort of the call's P pairs by expert: per-expert counts (shared
+// atomics), a scan over the experts for each expert's first list position and
+// unique index, then every pair takes the next place of its expert.  The
+// experts appear in ascending order; the order of one expert's pairs is the
+// order their atomics ran, which changes no output bit (each pair's row is
+// computed on its own, and the combine indexes rows by pair).
+constexpr int kRouteThreads = 1024;
+constexpr int kRouteMaxExperts = 1024;
+constexpr int kRouteBatch = 16;  // ids per thread in flight at once
+struct RouteArgs {
+    const void *ids;
+    int ids64, P, E, count_forward;
+    const int32_t *emap;
+    int64_t *hdr;
+    int32_t *dev_hdr;
+    int32_t *u_off, *u_pairs, *u_slot, *nu;
+};
+
+// Routed id of pair p: the expert, or -1 when outside [0, E).
+__device__ __forceinline__ int route_id(const RouteArgs &r, int p) {
+    const long long e = load_id64(r.ids, r.ids64, p);
+    return (e < 0 || e >= r.E) ? -1 : (int)e;
+}
+
+__device__ __forceinline__ int block_excl_scan(int v, int *s_warp, int &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < (int)(blockDim.x >> 5) ? s_warp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += t;
+        }
+        s_warp[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    total = s_warp[(blockDim.x >> 5) - 1];
+    const int before = warp > 0 ? s_warp[warp - 1] : 0;
+    __syncthreads();  // s_warp is reused by the next scan
+    return before + inc - v;
+}
+
+__global__ void __launch_bounds__(kRouteThreads, 1) prefill_route_kernel(const RouteArgs r) {
+    __shared__ int cnt[kRouteMaxExperts];   // pairs of each expert, then its next free place
+    __shared__ int s_warp[32];
+    __shared__ int s_bad;
+    const int E = r.E, P = r.P, tid = threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int e = tid; e < E; e += kRouteThreads) cnt[e] = 0;
+    if (tid == 0) s_bad = 0;
+    __syncthreads();
+    for (int c0 = 0; c0 < P; c0 += kRouteThreads * kRouteBatch) {
+        int ev[kRouteBatch];
+#pragma unroll
+        for (int j = 0; j < kRouteBatch; ++j) {
+            const int p = c0 + j * kRouteThreads + tid;
+            ev[j] = p < P ? route_id(r, p) : -2;
+        }
+#pragma unroll
+        for (int j = 0; j < kRouteBatch; ++j) {
+            if (ev[j] == -1)
+                s_bad = 1;
+            else if (ev[j] >= 0)
+                atomicAdd(&cnt[ev[j]], 1);
+        }
+    }
+    __syncthreads();
+    if (s_bad) {  // nothing is written but the status: the call's other kernels then do nothing
+        if (tid == 0) *reinterpret_cast<volatile int32_t *>(r.dev_hdr + kHdrStatus) = WISP_ERR_BAD_EXPERT;
+        return;
+    }
+    const int tot = tid < E ? cnt[tid] : 0;
+    int nu = 0, ptot = 0;
+    const int u = block_excl_scan(tot > 0 ? 1 : 0, s_warp, nu);
+    const int off = block_excl_scan(tot, s_warp, ptot);
+    if (tid < E) {
+        cnt[tid] = off;
+        if (tot > 0) {
+            r.u_off[u] = off;
+            r.u_slot[u] = r.emap[tid];
+        }
+    }
+    if (tid == 0) {
+        r.u_off[nu] = P;
+        *r.nu = nu;
+        r.dev_hdr[kHdrGroups] = 1;
+        r.dev_hdr[kHdrMisses] = 0;
+        r.dev_hdr[kHdrUnique] = nu;
+        if (r.count_forward) r.hdr[1] += 1;  // the forward (resident layers count only that)
+        r.hdr[5] += 1;                       // telemetry: groups, unique experts
+        r.hdr[6] += nu;
+        r.dev_hdr[kHdrStatus] = WISP_OK;
+    }
+    __syncthreads();
+    for (int c0 = 0; c0 < P; c0 += kRouteThreads * kRouteBatch) {
+        int ev[kRouteBatch];
+#pragma unroll
+        for (int j = 0; j < kRouteBatch; ++j) {
+            const int p = c0 + j * kRouteThreads + tid;
+            ev[j] = p < P ? route_id(r, p) : -2;
+        }
+#pragma unroll
+        for (int j = 0; j < kRouteBatch; ++j)
+            if (ev[j] >= 0) r.u_pairs[atomicAdd(&cnt[ev[j]], 1)] = c0 + j * kRouteThreads + tid;
+    }
 }
 
 // The group's experts and their 128-pair tiles, in shared memory.
@@ -131,6 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ Ring R;
     __shared__ TileTable tt;
     unsigned char *stages = align1024(smem_raw);
+    pdl_wait();
+    pdl_launch_dependents();
     const int I = g.I, n_cols = I / kHalfN;
     const int ntiles = gemm_setup(g, n_cols, tt, R);
     if (ntiles == 0) return;
@@ -194,6 +316,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ Ring R;
     __shared__ TileTable tt;
     unsigned char *stages = align1024(smem_raw);
+    pdl_wait();
+    pdl_launch_dependents();
     const int H = g.H, n_cols = H / kBN;
     const int ntiles = gemm_setup(g, n_cols, tt, R);
     if (ntiles == 0) return;
@@ -247,6 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // out[t] = sum over k in routing order of y[t * K + k], t in [t0, t1).
 __global__ void combine_kernel(const uint4 *y, int t0, int t1, int K, int H8, uint4 *out,
                                const int32_t *pager_status) {
+    pdl_wait();
+    pdl_launch_dependents();
     if (pager_status && *reinterpret_cast<const volatile int32_t *>(pager_status) != WISP_OK) return;
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long)(t1 - t0) * H8) return;
@@ -308,21 +434,17 @@ int launch_gather(const PrefillGroup &p, cudaStream_t stream) {
     const int warps = 8;
     const int blocks = (p.npairs + warps - 1) / warps;
     if (blocks <= 0) return WISP_OK;
-    gather_kernel<<<blocks, warps * 32, 0, stream>>>(reinterpret_cast<const uint4 *>(p.x), p.u_pairs, p.npairs, p.K,
-                                                     p.H / 8, reinterpret_cast<uint4 *>(p.x_perm), p.pager_status,
-                                                     p.status);
-    WISP_CUDA_TRY(cudaGetLastError());
-    return WISP_OK;
+    return launch_chained(gather_kernel, dim3(blocks), dim3(warps * 32), 0, stream,
+                          reinterpret_cast<const uint4 *>(p.x), p.u_pairs, p.npairs, p.K, p.H / 8,
+                          reinterpret_cast<uint4 *>(p.x_perm), p.pager_status, p.status);
 }
 
 int launch_combine(const PrefillGroup &p, cudaStream_t stream) {
     const long n = (long)(p.t1 - p.t0) * (p.H / 8);
     if (n <= 0) return WISP_OK;
-    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-        reinterpret_cast<const uint4 *>(p.y), p.t0, p.t1, p.K, p.H / 8, reinterpret_cast<uint4 *>(p.out),
-        p.pager_status);
-    WISP_CUDA_TRY(cudaGetLastError());
-    return WISP_OK;
+    return launch_chained(combine_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, stream,
+                          reinterpret_cast<const uint4 *>(p.y), p.t0, p.t1, p.K, p.H / 8,
+                          reinterpret_cast<uint4 *>(p.out), p.pager_status);
 }
 
 }  // namespace gemm
@@ -373,12 +495,36 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
     const int grid_gu = (int)std::min<long>(mtiles * (p.I / kHalfN), sms);
     const int grid_dn = (int)std::min<long>(mtiles * (p.H / kBN), sms);
     rc = launch_gather(p, stream);
-    if (rc) return rc;
-    gateup_gemm_kernel<<<grid_gu, kThreads, kSmemBytes, stream>>>(mx, mw13, g);
-    WISP_CUDA_TRY(cudaGetLastError());
-    down_gemm_kernel<<<grid_dn, kThreads, kSmemBytes, stream>>>(mact, mw2, g);
-    WISP_CUDA_TRY(cudaGetLastError());
-    return launch_combine(p, stream);
+    if (!rc)
+        rc = launch_chained(gateup_gemm_kernel, dim3(grid_gu), dim3(kThreads), (size_t)kSmemBytes, stream, mx, mw13, g);
+    if (!rc)
+        rc = launch_chained(down_gemm_kernel, dim3(grid_dn), dim3(kThreads), (size_t)kSmemBytes, stream, mact, mw2, g);
+    return rc ? rc : launch_combine(p, stream);
+}
+
+int launch_prefill_resident(const PrefillGroup &p, const BatchRoute &r, const PrefillLists &lists,
+                            cudaStream_t stream) {
+    using namespace gemm;
+    if (!prefill_shapes_supported(p.H, p.I))
+        return set_error("wisp: prefill GEMM needs hidden % 256 == 0 and inter % 128 == 0"), WISP_ERR_UNSUPPORTED;
+    if (p.npairs <= 0) return WISP_OK;
+    if (r.E < 1 || r.E > kRouteMaxExperts)
+        return set_error("wisp: resident routing takes at most 1024 experts"), WISP_ERR_INVALID;
+    RouteArgs a{};
+    a.ids = r.ids;
+    a.ids64 = r.ids64;
+    a.P = p.npairs;
+    a.E = r.E;
+    a.count_forward = r.count_forward;
+    a.emap = r.emap;
+    a.hdr = r.hdr;
+    a.dev_hdr = r.dev_status;
+    a.u_off = lists.u_off;
+    a.u_pairs = lists.u_pairs;
+    a.u_slot = lists.u_slot;
+    a.nu = lists.nu;
+    int rc = launch_chained(prefill_route_kernel, dim3(1), dim3(kRouteThreads), 0, stream, a);
+    return rc ? rc : launch_prefill_group(p, stream);
 }
 
 }  // namespace wisp

@@ -826,14 +826,23 @@ int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w,
         WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
         return WISP_OK;
     }
-    PagerParams p;
-    fill_pager_params(L, p, ids, ids64, T, K, 0, 1);
-    int rc = launch_pager(p, stream);
-    if (rc) return rc;
-    ++L->launches;
+    // token-major GEMMs: a routing kernel writes the group lists, as the pager
+    // would for an all-resident call, and counts the forward (no LRU state: a
+    // resident layer pages nothing)
+    BatchRoute r{};
+    r.ids = ids;
+    r.ids64 = ids64;
+    r.E = L->E;
+    r.count_forward = 1;
+    r.emap = L->d_emap;
+    r.hdr = L->d_hdr;
+    r.dev_status = L->d_dev_hdr + kHdrStatus;
+    PrefillLists lists{L->d_u_off, L->d_u_pairs, L->d_u_slot, L->d_grp_nu};
     const int nu_bound = (int)std::min<long>(L->E, (long)T * K);
-    rc = launch_tc_group(L, path, tc_group(L, x, w, out, 0, 0, T, K, nu_bound, L->d_dev_hdr + kHdrStatus), stream);
+    const int rc = launch_prefill_resident(tc_group(L, x, w, out, 0, 0, T, K, nu_bound, L->d_dev_hdr + kHdrStatus),
+                                           r, lists, stream);
     if (rc) return rc;
+    L->launches += kPrefillKernelsResident;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
     return WISP_OK;
 }
