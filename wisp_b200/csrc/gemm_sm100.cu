@@ -38,23 +38,39 @@ __global__ void gather_kernel(const uint4 *x, const int32_t *u_pairs, int P, int
     for (int c = threadIdx.x & 31; c < H8; c += 32) dst[c] = src[c];
 }
 
-// ---- routing of a resident call (one block) --------------------------------------
-// Counting sort of the call's P pairs by expert: per-expert counts (shared
-// atomics), a scan over the experts for each expert's first list position and
-// unique index, then every pair takes the next place of its expert.  The
-// experts appear in ascending order; the order of one expert's pairs is the
-// order their atomics ran, which changes no output bit (each pair's row is
-// computed on its own, and the combine indexes rows by pair).
+// ---- routing and gather of a resident call (one cooperative launch) ---------------
+// Counting sort of the call's P pairs by expert, fused with the gather of
+// their token rows.  Block b takes the contiguous pairs [b R, (b + 1) R):
+//   1. counts them per expert in shared memory and adds the counts to the
+//      launch's global per-expert counters (ids outside [0, E) raise a flag);
+//   2. grid barrier;
+//   3. every block scans the global counts over the experts (first list
+//      position of each expert; block 0 writes the lists' header: offsets,
+//      slots, the expert count, the header words and the forward's count);
+//      each block reserves its run inside every expert's range with one
+//      global atomic per expert it holds, then places its pairs (shared
+//      atomics) and copies their token rows x[t] to X_perm[position].
+// The experts appear in ascending order; the order of one expert's pairs is
+// the order the atomics ran, which changes no output bit (each pair's row is
+// computed on its own, and the combine indexes rows by pair).  The counters
+// come in two halves by launch parity: a launch uses one (zero on entry) and
+// zeroes the other for the next launch.
 constexpr int kRouteThreads = 1024;
 constexpr int kRouteMaxExperts = 1024;
-constexpr int kRouteBatch = 16;  // ids per thread in flight at once
+constexpr int kRouteExpertsPerThread = kRouteMaxExperts / kRouteThreads;
 struct RouteArgs {
     const void *ids;
-    int ids64, P, E, count_forward;
+    int ids64, P, E, K, H8, count_forward;
     const int32_t *emap;
+    const uint4 *x;
+    uint4 *x_perm;
     int64_t *hdr;
     int32_t *dev_hdr;
+    int *status;                      // sticky status word
     int32_t *u_off, *u_pairs, *u_slot, *nu;
+    int32_t *cnt, *cnt_next;          // [2 E + 1]: counts, fills, bad-id flag
+    uint32_t *bar;                    // [2]: arrivals, generation (self-resetting)
+    long long wait_ns;
 };
 
 // Routed id of pair p: the expert, or -1 when outside [0, E).
@@ -89,48 +105,99 @@ __device__ __forceinline__ int block_excl_scan(int v, int *s_warp, int &total) {
     return before + inc - v;
 }
 
-__global__ void __launch_bounds__(kRouteThreads, 1) prefill_route_kernel(const RouteArgs r) {
-    __shared__ int cnt[kRouteMaxExperts];   // pairs of each expert, then its next free place
+// Every block; false when the wait ran out (then the status word says so).
+__device__ bool route_grid_barrier(const RouteArgs &r) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        volatile uint32_t *vgen = r.bar + 1;
+        const uint32_t gen = *vgen;
+        __threadfence();
+        int ok = 1;
+        if (atomicAdd(r.bar, 1u) == gridDim.x - 1) {
+            atomicExch(r.bar, 0u);
+            __threadfence();
+            atomicAdd(r.bar + 1, 1u);
+        } else {
+            const unsigned long long t0 = globaltimer_ns();
+            while (*vgen == gen) {
+                if ((long long)(globaltimer_ns() - t0) > r.wait_ns) {
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+__global__ void __launch_bounds__(kRouteThreads, 1) route_gather_kernel(const RouteArgs r) {
+    extern __shared__ int2 route_list[];  // this block's (pair, expert), then (pair, position)
+    __shared__ int hist[kRouteMaxExperts];  // this block's pairs per expert, then its next place
+    __shared__ int eoff[kRouteMaxExperts];
     __shared__ int s_warp[32];
     __shared__ int s_bad;
     const int E = r.E, P = r.P, tid = threadIdx.x;
     pdl_wait();
     pdl_launch_dependents();
-    for (int e = tid; e < E; e += kRouteThreads) cnt[e] = 0;
+    const int R = (P + gridDim.x - 1) / gridDim.x;
+    const int p_lo = min(P, (int)blockIdx.x * R), p_hi = min(P, p_lo + R), n = p_hi - p_lo;
+    for (int e = tid; e < E; e += kRouteThreads) hist[e] = 0;
+    for (int i = blockIdx.x * kRouteThreads + tid; i < 2 * E + 1; i += gridDim.x * kRouteThreads)
+        r.cnt_next[i] = 0;
     if (tid == 0) s_bad = 0;
     __syncthreads();
-    for (int c0 = 0; c0 < P; c0 += kRouteThreads * kRouteBatch) {
-        int ev[kRouteBatch];
-#pragma unroll
-        for (int j = 0; j < kRouteBatch; ++j) {
-            const int p = c0 + j * kRouteThreads + tid;
-            ev[j] = p < P ? route_id(r, p) : -2;
-        }
-#pragma unroll
-        for (int j = 0; j < kRouteBatch; ++j) {
-            if (ev[j] == -1)
-                s_bad = 1;
-            else if (ev[j] >= 0)
-                atomicAdd(&cnt[ev[j]], 1);
-        }
+    for (int i = tid; i < n; i += kRouteThreads) {
+        const int e = route_id(r, p_lo + i);
+        route_list[i] = make_int2(p_lo + i, e);
+        if (e < 0)
+            s_bad = 1;
+        else
+            atomicAdd(&hist[e], 1);
     }
     __syncthreads();
-    if (s_bad) {  // nothing is written but the status: the call's other kernels then do nothing
-        if (tid == 0) *reinterpret_cast<volatile int32_t *>(r.dev_hdr + kHdrStatus) = WISP_ERR_BAD_EXPERT;
-        return;
-    }
-    const int tot = tid < E ? cnt[tid] : 0;
-    int nu = 0, ptot = 0;
-    const int u = block_excl_scan(tot > 0 ? 1 : 0, s_warp, nu);
-    const int off = block_excl_scan(tot, s_warp, ptot);
-    if (tid < E) {
-        cnt[tid] = off;
-        if (tot > 0) {
-            r.u_off[u] = off;
-            r.u_slot[u] = r.emap[tid];
+    if (s_bad && tid == 0) atomicOr(r.cnt + 2 * E, 1);
+    for (int e = tid; e < E; e += kRouteThreads)
+        if (hist[e]) atomicAdd(r.cnt + e, hist[e]);
+    const bool synced = route_grid_barrier(r);
+    if (!synced || *reinterpret_cast<volatile int32_t *>(r.cnt + 2 * E)) {
+        if ((blockIdx.x == 0 || !synced) && tid == 0) {  // a block whose wait ran out reports it itself
+            const int code = synced ? WISP_ERR_BAD_EXPERT : WISP_ERR_TIMEOUT;
+            *reinterpret_cast<volatile int32_t *>(r.dev_hdr + kHdrStatus) = code;
+            if (r.status) *reinterpret_cast<volatile int *>(r.status) = code;
         }
+        return;  // the call's other kernels see the status and do nothing
     }
-    if (tid == 0) {
+    // experts [4 tid, 4 tid + 4): counts, then offsets and unique indices by block scans
+    int c[kRouteExpertsPerThread], f = 0, sum = 0;
+#pragma unroll
+    for (int j = 0; j < kRouteExpertsPerThread; ++j) {
+        const int e = tid * kRouteExpertsPerThread + j;
+        c[j] = e < E ? __ldcg(r.cnt + e) : 0;
+        sum += c[j];
+        f += c[j] > 0;
+    }
+    int nu = 0, ptot = 0;
+    int u = block_excl_scan(f, s_warp, nu);
+    int off = block_excl_scan(sum, s_warp, ptot);
+#pragma unroll
+    for (int j = 0; j < kRouteExpertsPerThread; ++j) {
+        const int e = tid * kRouteExpertsPerThread + j;
+        if (e < E) {
+            eoff[e] = off;
+            if (blockIdx.x == 0 && c[j] > 0) {
+                r.u_off[u] = off;
+                r.u_slot[u] = r.emap[e];
+            }
+        }
+        off += c[j];
+        u += c[j] > 0;
+    }
+    if (blockIdx.x == 0 && tid == 0) {
         r.u_off[nu] = P;
         *r.nu = nu;
         r.dev_hdr[kHdrGroups] = 1;
@@ -142,16 +209,37 @@ __global__ void __launch_bounds__(kRouteThreads, 1) prefill_route_kernel(const R
         r.dev_hdr[kHdrStatus] = WISP_OK;
     }
     __syncthreads();
-    for (int c0 = 0; c0 < P; c0 += kRouteThreads * kRouteBatch) {
-        int ev[kRouteBatch];
+    // this block's run inside each expert's range
+    for (int e = tid; e < E; e += kRouteThreads)
+        if (hist[e]) hist[e] = eoff[e] + atomicAdd(r.cnt + E + e, hist[e]);
+    __syncthreads();
+    for (int i = tid; i < n; i += kRouteThreads) {
+        const int2 pe = route_list[i];
+        const int pos = atomicAdd(&hist[pe.y], 1);
+        r.u_pairs[pos] = pe.x;
+        route_list[i] = make_int2(pe.x, pos);
+    }
+    __syncthreads();
+    // token rows: the block's n rows x H8 16-byte words, all threads, 4 in flight each
+    const int H8 = r.H8, K = r.K;
+    const long total = (long)n * H8;
+    for (long i0 = tid; i0 < total; i0 += 4L * kRouteThreads) {
+        uint4 v[4];
+        long dst[4];
 #pragma unroll
-        for (int j = 0; j < kRouteBatch; ++j) {
-            const int p = c0 + j * kRouteThreads + tid;
-            ev[j] = p < P ? route_id(r, p) : -2;
+        for (int j = 0; j < 4; ++j) {
+            const long i = i0 + (long)j * kRouteThreads;
+            dst[j] = -1;
+            if (i < total) {
+                const int row = (int)(i / H8), w = (int)(i - (long)row * H8);
+                const int2 pp = route_list[row];
+                v[j] = __ldg(r.x + (size_t)(pp.x / K) * H8 + w);
+                dst[j] = (long)pp.y * H8 + w;
+            }
         }
 #pragma unroll
-        for (int j = 0; j < kRouteBatch; ++j)
-            if (ev[j] >= 0) r.u_pairs[atomicAdd(&cnt[ev[j]], 1)] = c0 + j * kRouteThreads + tid;
+        for (int j = 0; j < 4; ++j)
+            if (dst[j] >= 0) r.x_perm[dst[j]] = v[j];
     }
 }
 
@@ -453,7 +541,8 @@ bool prefill_shapes_supported(int H, int I) {
     return H > 0 && I > 0 && H % gemm::kBN == 0 && I % gemm::kHalfN == 0;
 }
 
-int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
+namespace {
+int launch_prefill_kernels(const PrefillGroup &p, bool gather, cudaStream_t stream) {
     using namespace gemm;
     if (!prefill_shapes_supported(p.H, p.I))
         return set_error("wisp: prefill GEMM needs hidden % 256 == 0 and inter % 128 == 0"), WISP_ERR_UNSUPPORTED;
@@ -494,13 +583,18 @@ int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) {
     const long mtiles = (long)p.nu + (p.npairs + kBM - 1) / kBM;
     const int grid_gu = (int)std::min<long>(mtiles * (p.I / kHalfN), sms);
     const int grid_dn = (int)std::min<long>(mtiles * (p.H / kBN), sms);
-    rc = launch_gather(p, stream);
+    if (gather) rc = launch_gather(p, stream);
     if (!rc)
         rc = launch_chained(gateup_gemm_kernel, dim3(grid_gu), dim3(kThreads), (size_t)kSmemBytes, stream, mx, mw13, g);
     if (!rc)
         rc = launch_chained(down_gemm_kernel, dim3(grid_dn), dim3(kThreads), (size_t)kSmemBytes, stream, mact, mw2, g);
     return rc ? rc : launch_combine(p, stream);
 }
+
+int launch_prefill_gemms(const PrefillGroup &p, cudaStream_t stream) { return launch_prefill_kernels(p, false, stream); }
+}  // namespace
+
+int launch_prefill_group(const PrefillGroup &p, cudaStream_t stream) { return launch_prefill_kernels(p, true, stream); }
 
 int launch_prefill_resident(const PrefillGroup &p, const BatchRoute &r, const PrefillLists &lists,
                             cudaStream_t stream) {
@@ -510,21 +604,46 @@ int launch_prefill_resident(const PrefillGroup &p, const BatchRoute &r, const Pr
     if (p.npairs <= 0) return WISP_OK;
     if (r.E < 1 || r.E > kRouteMaxExperts)
         return set_error("wisp: resident routing takes at most 1024 experts"), WISP_ERR_INVALID;
+    if (!lists.cnt || !lists.cnt_next || !lists.bar)
+        return set_error("wisp: resident routing without its counters"), WISP_ERR_INVALID;
+    int dev = 0, sms = 0;
+    WISP_CUDA_TRY(cudaGetDevice(&dev));
+    WISP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int blocks = std::max(1, std::min(sms, (p.npairs + 63) / 64));
+    const int per = (p.npairs + blocks - 1) / blocks;
+    const size_t smem = sizeof(int2) * (size_t)per;
+    if (smem > 160 * 1024) return set_error("wisp: resident call too large for one routing launch"), WISP_ERR_INVALID;
+    static size_t smem_set[64] = {};
+    if (dev < 0 || dev >= 64) return WISP_ERR_INVALID;
+    if (smem_set[dev] < smem) {
+        WISP_CUDA_TRY(cudaFuncSetAttribute(route_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem));
+        smem_set[dev] = smem;
+    }
     RouteArgs a{};
     a.ids = r.ids;
     a.ids64 = r.ids64;
     a.P = p.npairs;
     a.E = r.E;
+    a.K = p.K;
+    a.H8 = p.H / 8;
     a.count_forward = r.count_forward;
     a.emap = r.emap;
+    a.x = reinterpret_cast<const uint4 *>(p.x);
+    a.x_perm = reinterpret_cast<uint4 *>(p.x_perm);
     a.hdr = r.hdr;
     a.dev_hdr = r.dev_status;
+    a.status = p.status;
     a.u_off = lists.u_off;
     a.u_pairs = lists.u_pairs;
     a.u_slot = lists.u_slot;
     a.nu = lists.nu;
-    int rc = launch_chained(prefill_route_kernel, dim3(1), dim3(kRouteThreads), 0, stream, a);
-    return rc ? rc : launch_prefill_group(p, stream);
+    a.cnt = lists.cnt;
+    a.cnt_next = lists.cnt_next;
+    a.bar = lists.bar;
+    a.wait_ns = p.wait_ns;
+    int rc = launch_persistent(route_gather_kernel, dim3(blocks), dim3(kRouteThreads), smem, stream, a);
+    return rc ? rc : launch_prefill_gemms(p, stream);
 }
 
 }  // namespace wisp

@@ -161,6 +161,8 @@ struct wisp_layer {
     uint32_t *d_ready = nullptr;     // weight-stationary path: per-token-block counters, two halves
     uint32_t *d_combined = nullptr;  // weight-stationary path: per-token combine counters, two halves
     int ready_parity = 0;            // the halves the next weight-stationary launch uses
+    int32_t *d_route = nullptr;      // resident prefill routing: two halves of 2 E + 1 counters, 2 barrier words
+    int route_parity = 0;
     int tc_min_pairs = kPrefillMinPairs;  // calls of at least this many pairs run on the tensor cores
     int compute_class = 0;           // 0: by call size; 1: CUDA-core kernels; 2: tensor cores
     bool primed = false;             // resident layer: every expert copied into its slot
@@ -377,7 +379,8 @@ void free_ws(wisp_layer *L) {
                     (void *)L->d_grp_nhit, (void *)L->d_u_slot,
                     (void *)L->d_u_gen, (void *)L->d_u_off, (void *)L->d_u_pairs, (void *)L->d_counters,
                     (void *)L->d_dev_hdr, (void *)L->d_act, (void *)L->d_y, (void *)L->d_xperm,
-                    (void *)L->d_actperm, (void *)L->d_ready, (void *)L->d_combined, (void *)L->d_xq,
+                    (void *)L->d_actperm, (void *)L->d_ready, (void *)L->d_combined, (void *)L->d_route,
+                    (void *)L->d_xq,
                     (void *)L->d_aq, (void *)L->d_xs, (void *)L->d_as})
         cudaFree(p);
     L->d_xq = L->d_aq = nullptr;
@@ -387,6 +390,7 @@ void free_ws(wisp_layer *L) {
         L->d_u_pairs = L->d_counters = L->d_dev_hdr = nullptr;
     L->d_act = L->d_y = L->d_xperm = L->d_actperm = nullptr;
     L->d_ready = L->d_combined = nullptr;
+    L->d_route = nullptr;
     L->h_mb = L->d_mb = nullptr;
     L->wsT = -1;
     L->wsK = 0;
@@ -437,6 +441,10 @@ int ensure_ws(wisp_layer *L, int T, int K) {
             WISP_CUDA_TRY(cudaMalloc(&L->d_combined, sizeof(uint32_t) * 2 * batch_done_words(L->H)));
             WISP_CUDA_TRY(cudaMemset(L->d_combined, 0, sizeof(uint32_t) * 2 * batch_done_words(L->H)));
             L->ready_parity = 0;
+            const size_t rw = 2 * (2 * (size_t)L->E + 1) + 2;
+            WISP_CUDA_TRY(cudaMalloc(&L->d_route, sizeof(int32_t) * rw));
+            WISP_CUDA_TRY(cudaMemset(L->d_route, 0, sizeof(int32_t) * rw));
+            L->route_parity = 0;
         }
     }
     const long words = (mailbox_words(nT, nK) + 31) & ~31L;
@@ -837,11 +845,15 @@ int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w,
     r.emap = L->d_emap;
     r.hdr = L->d_hdr;
     r.dev_status = L->d_dev_hdr + kHdrStatus;
-    PrefillLists lists{L->d_u_off, L->d_u_pairs, L->d_u_slot, L->d_grp_nu};
+    const size_t half = 2 * (size_t)L->E + 1;
+    PrefillLists lists{L->d_u_off, L->d_u_pairs, L->d_u_slot, L->d_grp_nu,
+                       L->d_route + L->route_parity * half, L->d_route + (L->route_parity ^ 1) * half,
+                       reinterpret_cast<uint32_t *>(L->d_route + 2 * half)};
     const int nu_bound = (int)std::min<long>(L->E, (long)T * K);
     const int rc = launch_prefill_resident(tc_group(L, x, w, out, 0, 0, T, K, nu_bound, L->d_dev_hdr + kHdrStatus),
                                            r, lists, stream);
     if (rc) return rc;
+    L->route_parity ^= 1;
     L->launches += kPrefillKernelsResident;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
     return WISP_OK;

@@ -79,20 +79,25 @@ struct BatchRoute {
 constexpr int kBatchKernelsResident = 1;
 int launch_batch_resident(const PrefillGroup &p, const BatchRoute &r, const BatchCounters &c, cudaStream_t stream);
 
-// A whole call of a resident layer on the token-major GEMMs: one routing
+// A whole call of a resident layer on the token-major GEMMs: one cooperative
 // kernel writes the group lists the GEMMs read (the pairs sorted by expert,
 // experts ascending; each expert's slot from the map; the count into *nu and
-// the group header words) and counts the forward
-// as the weight-stationary path does, then gather, gate-up, down and combine
-// run on them.  p.u_off / u_pairs / u_slot / nu_dev must be the addresses the
-// routing kernel writes (`lists`); r.dev_status is the group header (status
-// word first).  A routed id outside [0, E) leaves the lists alone, records
-// WISP_ERR_BAD_EXPERT in the header and the sticky word, and the other
-// kernels of the call then do nothing.
+// the group header words), gathers the pairs' token rows into X_perm and
+// counts the forward as the weight-stationary path does; then gate-up, down
+// and combine run on them.  p.u_off / u_pairs / u_slot / nu_dev must be the
+// addresses the routing kernel writes (`lists`); r.dev_status is the group
+// header (status word first).  `cnt` / `cnt_next`: the routing counters of
+// this launch and of the next (2 E + 1 words each, two halves by launch
+// parity); `bar`: two words of the kernel's grid barrier.  A routed id
+// outside [0, E) leaves the lists alone, records WISP_ERR_BAD_EXPERT in the
+// header and the sticky word, and the other kernels of the call then do
+// nothing.
 struct PrefillLists {
     int32_t *u_off, *u_pairs, *u_slot, *nu;
+    int32_t *cnt, *cnt_next;
+    uint32_t *bar;
 };
-constexpr int kPrefillKernelsResident = kPrefillKernelsPerGroup + 1;
+constexpr int kPrefillKernelsResident = kPrefillKernelsPerGroup;
 int launch_prefill_resident(const PrefillGroup &p, const BatchRoute &r, const PrefillLists &lists,
                             cudaStream_t stream);
 
