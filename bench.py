@@ -307,29 +307,56 @@ def algorithmic_bytes(unique_experts: int, tokens: int, launches: int, shape=Non
             + tokens * shape.top_k * (4 + 4)) if launches else 0
 
 
-def paged_point(masters, dev, shape, B, C, routes, x, warmup, steps, hbm_peak, h2d, layers=None):
+def paged_point(masters, dev, shape, B, C, routes, x, warmup, steps, hbm_peak, h2d, layers=None,
+                prefetch=None):
     """Decode (or prefill) of a paged stack at cap C: ``routes[s][layer] =
     (ids, w)`` on the device, ``x`` [B, H]; warm-up steps untimed, then
     ``steps`` timed with CUDA events.  Returns the point's figures: tok/s
     of the stack of ``layers`` layers (default: as many as masters),
     page-in GB/s against the measured H2D peak and the step roofline (the
     slower of the HBM bytes at the HBM peak and the page-in bytes at the H2D
-    peak, over the measured time)."""
+    peak, over the measured time).
+
+    ``prefetch``: a co-occurrence table (the reference's cross-layer
+    prefetch, fused_moe.py:1170-1233): after each layer's forward the
+    experts it routed to are recorded for the step, max(8, C // 2) experts
+    are predicted for the next layer (normalised scores, decay 0.5) and
+    paged into it speculatively on its copy stream, and each finished step
+    is learned online; the host work is inside the timed region, as in the
+    reference."""
     from wisp_b200.integrations.vllm.fused_moe import WispMoEState
     L = len(masters)
     states = [WispMoEState(h13, h2, C, "paged", dev, i) for i, (h13, h2) in enumerate(masters)]
     out = torch.empty_like(x)
-    for s in range(warmup):
+    seen = None
+    if prefetch is not None:
+        from wisp_b200.integrations.vllm.cooccur import predict_layer
+        seen = [[sorted(set(routes[s][li][0].reshape(-1).tolist())) for li in range(L)]
+                for s in range(warmup + steps)]
+
+    def step(s):
+        obs = {}
         for li in range(L):
             states[li].forward(x, routes[s][li][1], routes[s][li][0], out=out)
+            if prefetch is None:
+                continue
+            obs[li] = seen[s][li]
+            if li + 1 < L:
+                pred = predict_layer(prefetch, obs, li + 1, k=max(8, C // 2), normalize=True, decay=0.5)
+                if pred:
+                    states[li + 1].prefetch_async(set(pred))
+        if prefetch is not None:
+            prefetch.observe_step(obs)
+
+    for s in range(warmup):
+        step(s)
     torch.cuda.synchronize()
     tel0 = [st.telemetry() for st in states]
     st0 = [st.stats() for st in states]
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for s in range(warmup, warmup + steps):
-        for li in range(L):
-            states[li].forward(x, routes[s][li][1], routes[s][li][0], out=out)
+        step(s)
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
@@ -417,6 +444,18 @@ def sweep_phase(masters, dev, hbm_peak, h2d):
         x = wl.hidden_states(B, q.hidden, seed=B).to(dev)
         for C in (8, 16, 24, 32):
             out[f"cfg1_b{B}_cap{C}"] = paged_point(masters, dev, q, B, C, routes, x, warm, steps, hbm_peak, h2d)
+        if B == 16:
+            # the reference's cross-layer prefetch on the B200 link (off by default
+            # there too): a table learned online, warmed on 7 other steps of the
+            # same routing process (same per-layer popularity, other draws)
+            from wisp_b200.integrations.vllm.cooccur import CooccurTable
+            table = CooccurTable()
+            wids, _ = wl.zipf_trace(12, L, B, q.experts, q.top_k, 1.1, 0.6, seed=11 + B)
+            for s in range(5, 12):
+                table.observe_step({li: sorted(set(wids[s, li].reshape(-1).tolist())) for li in range(L)})
+            r = paged_point(masters, dev, q, B, 32, routes, x, warm, steps, hbm_peak, h2d, prefetch=table)
+            r["prefetch"] = "co-occurrence table, online, predict max(8, cap // 2) for the next layer"
+            out["cfg1_b16_cap32_prefetch"] = r
     # prefill chunks of 2048 tokens per sequence, batch 1 and 4, cap 32
     for B, nl in ((1, 2), (4, 1)):
         T = 2048 * B
@@ -546,9 +585,15 @@ def run_wisp(args):
     del states
     torch.cuda.empty_cache()
     res = {}
+    prefill = None
     if not args.no_resident:
         for rb in sorted({B, 4, 1}, reverse=True):
             res[f"batch{rb}"] = resident_phase(args, masters, dev, hbm_peak, rb)
+        # configs[2]'s 2048-token chunk on resident layers: the tensor-core prefill path alone
+        pa = argparse.Namespace(**vars(args))
+        pa.steps, pa.warmup = 4, 2
+        prefill = prefill_only(pa, dev, hbm_peak, peak_src, masters=masters[:8])["prefill"]
+        torch.cuda.empty_cache()
     sweep = None
     if args.sweep and args.workload == "qwen3-30b":
         t_sw = time.time()
@@ -591,6 +636,7 @@ def run_wisp(args):
         "pagein": {"gbs": pagein_gbs, "h2d_peak_gbs": h2d, "frac": pagein_gbs / h2d,
                    "misses": misses, "hits": hits, "bytes": pagein_bytes},
         "resident_decode": res,
+        "resident_prefill": prefill,
         "configs": sweep,
         "e2e": e2e,
         "clocks": clk.summary(),
@@ -616,7 +662,7 @@ def resident_only(args, dev, hbm_peak, peak_src):
             "resident_decode": r}
 
 
-def prefill_only(args, dev, hbm_peak, peak_src):
+def prefill_only(args, dev, hbm_peak, peak_src, masters=None):
     """Config 3's prefill chunk on resident layers (cap = E): T = 2048 tokens,
     uniform top-8 of 128 (every expert touched), one forward per layer on the
     tcgen05 tensor-core path; reports tensor TFLOP/s (2 T k 3 H I per layer)
@@ -630,7 +676,8 @@ def prefill_only(args, dev, hbm_peak, peak_src):
         pass
     L = min(args.layers, 8)
     T = 2048
-    masters = make_masters(L, dev)
+    masters = masters if masters is not None else make_masters(L, dev)
+    L = min(L, len(masters))
     states = []
     for i in range(L):
         st = WispMoEState(masters[i][0], masters[i][1], SHAPE.experts, "resident", dev, i)
