@@ -220,26 +220,35 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_gather_kernel(const Ro
         route_list[i] = make_int2(pe.x, pos);
     }
     __syncthreads();
-    // token rows: the block's n rows x H8 16-byte words, all threads, 4 in flight each
-    const int H8 = r.H8, K = r.K;
-    const long total = (long)n * H8;
-    for (long i0 = tid; i0 < total; i0 += 4L * kRouteThreads) {
-        uint4 v[4];
-        long dst[4];
+    // token rows: warp w copies rows w, w + 32, ..., two rows at a time with
+    // up to 8 16-byte words of each in flight per lane (32-bit index arithmetic)
+    const int H8 = r.H8, K = r.K, lane = tid & 31, warp = tid >> 5;
+    constexpr int kWarpsR = kRouteThreads / 32;
+    for (int r0 = warp; r0 < n; r0 += 2 * kWarpsR) {
+        const int r1 = r0 + kWarpsR;
+        const int2 a = route_list[r0];
+        const int2 b = r1 < n ? route_list[r1] : make_int2(0, -1);
+        const uint4 *sa = r.x + (size_t)(a.x / K) * H8, *sb = r.x + (size_t)(b.x / K) * H8;
+        uint4 *da = r.x_perm + (size_t)a.y * H8, *db = r.x_perm + (size_t)(b.y < 0 ? 0 : b.y) * H8;
+        for (int w0 = lane; w0 < H8; w0 += 32 * 4) {
+            uint4 va[4], vb[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const long i = i0 + (long)j * kRouteThreads;
-            dst[j] = -1;
-            if (i < total) {
-                const int row = (int)(i / H8), w = (int)(i - (long)row * H8);
-                const int2 pp = route_list[row];
-                v[j] = __ldg(r.x + (size_t)(pp.x / K) * H8 + w);
-                dst[j] = (long)pp.y * H8 + w;
+            for (int j = 0; j < 4; ++j) {
+                const int w = w0 + 32 * j;
+                if (w < H8) {
+                    va[j] = __ldg(sa + w);
+                    if (b.y >= 0) vb[j] = __ldg(sb + w);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int w = w0 + 32 * j;
+                if (w < H8) {
+                    da[w] = va[j];
+                    if (b.y >= 0) db[w] = vb[j];
+                }
             }
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (dst[j] >= 0) r.x_perm[dst[j]] = v[j];
     }
 }
 
