@@ -273,18 +273,26 @@ def workload_name(args, world: int = 1) -> str:
                 f" per GPU, expert-parallel over {world} GPUs, cap {cap} per GPU")
 
 
-def profile_traffic(name: str):
+def profile_traffic(name: str, units: float | None = None):
     """DRAM bytes per launch of the dominant kernel from a committed ncu summary
-    (a line ``traffic_bytes_per_launch: N``), or None."""
+    (a line ``traffic_bytes_per_launch: N``), or None.  When the summary also
+    names the routed experts of the captured launch (``experts_per_captured_launch:
+    n``) and ``units`` gives the bench's experts per launch, the traffic is scaled
+    by that ratio (weight traffic grows in proportion to the routed experts)."""
     path = os.path.join(ROOT, "profiles", name)
+    vals = {}
     try:
         with open(path) as f:
             for line in f:
-                if line.strip().startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip().split()[0])
+                for key in ("traffic_bytes_per_launch", "experts_per_captured_launch"):
+                    if line.strip().startswith(key + ":"):
+                        vals[key] = float(line.split(":", 1)[1].strip().split()[0])
     except OSError:
         pass
-    return None
+    t = vals.get("traffic_bytes_per_launch")
+    if t is not None and units and vals.get("experts_per_captured_launch"):
+        t *= units / vals["experts_per_captured_launch"]
+    return t
 
 
 def dominant_kernel(batch: int, tc_min_pairs: int) -> str:
@@ -616,7 +624,10 @@ def run_wisp(args):
                               f"forward ({r['launches_per_forward']:.0f} launches) timed with CUDA events",
                     "achieved": r["hbm_gbs"], "peak": hbm_peak, "unit": "GB/s",
                     "frac": r["frac"], "peak_src": peak_src,
-                    "traffic": profile_traffic(f"{r['kernel']}_resident_decode_b{B}.md"),
+                    "traffic": profile_traffic(f"{r['kernel']}_resident_decode_b{B}.md",
+                                               r["unique_experts_per_forward"]),
+                    "traffic_note": "ncu DRAM read + write of one captured launch, scaled to this "
+                                    "run's routed experts per launch",
                     "bytes_per_forward": r["bytes_per_forward"], "us_per_forward": r["us_per_forward"]}
 
     line = {
