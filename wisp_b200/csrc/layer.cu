@@ -176,6 +176,12 @@ struct wisp_layer {
     std::atomic<uint32_t> flag_idx{0};
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_pager = nullptr, ev_copies = nullptr, ev_last = nullptr;
+    // resident forwards skip the two event waits when stream order already
+    // covers them: the last forward ran on the same stream and no copy was
+    // queued since that stream waited for the copies
+    cudaStream_t last_stream = nullptr;
+    bool last_stream_set = false;
+    uint64_t copy_gen = 0, copy_waited = ~0ull;
     std::vector<cudaEvent_t> ev_group, ev_copy;
     uint32_t seq = 0;
     bool async = true;
@@ -591,6 +597,7 @@ int run_pager(wisp_layer *L, const void *ids, int ids64, int T, int K, int singl
     if (rc) return rc;
     ++L->launches;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_pager, stream));
+    L->last_stream_set = false;
     WISP_CUDA_TRY(cudaEventSynchronize(L->ev_pager));
     const int status = ((volatile int32_t *)L->h_mb)[0];
     if (status == WISP_OK && count_forward && L->mode != WISP_MODE_RESIDENT) {
@@ -792,7 +799,9 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
         WISP_CUDA_TRY(cudaEventRecord(L->ev_group[g], stream));
     }
     WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
+    ++L->copy_gen;
     WISP_CUDA_TRY(cudaEventRecord(L->ev_last, stream));
+    L->last_stream_set = false;  // the next resident forward waits for this work explicitly
     return WISP_OK;
 }
 
@@ -803,6 +812,20 @@ int page_and_compute(wisp_layer *L, const void *x, const float *w, int T, int K,
 // expert lists and count on the device and the GEMM kernels read them there.
 // A rejected call is skipped and its status lands in the sticky word,
 // reported by the next call or synchronize.
+// Order `stream` after the layer's previous forward and its copies (the
+// workspace and the slots), unless stream order already does; then note the
+// stream as the layer's last.
+int order_resident(wisp_layer *L, cudaStream_t stream) {
+    if (!(L->last_stream_set && L->last_stream == stream && L->copy_waited == L->copy_gen)) {
+        WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));
+        WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
+        L->copy_waited = L->copy_gen;
+    }
+    L->last_stream = stream;
+    L->last_stream_set = true;
+    return WISP_OK;
+}
+
 int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w, const void *ids, int ids64,
                         int T, int K, void *out, cudaStream_t stream) {
     if (T > L->wsT || K > L->wsK) {
@@ -812,8 +835,8 @@ int forward_tc_resident(wisp_layer *L, Path path, const void *x, const float *w,
         if (rc) return rc;
     }
     // the layer's workspace: after its previous forward, whichever stream that used
-    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));
-    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
+    int orc = order_resident(L, stream);
+    if (orc) return orc;
     if (path == Path::kBatchTC) {
         BatchRoute r{};
         r.ids = ids;
@@ -915,8 +938,14 @@ int forward_async(wisp_layer *L, const void *x, const float *w, const void *ids,
     }
     fp.pg.mb = L->d_mb + (long)slot * L->mb_words;
     if (paged) L->last_unique_host = false;  // this forward's set is known on the device only
-    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));  // the workspace, whichever stream used it last
-    WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
+    if (paged) {
+        WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_last, 0));  // the workspace, whichever stream used it last
+        WISP_CUDA_TRY(cudaStreamWaitEvent(stream, L->ev_copies, 0));
+        L->last_stream_set = false;
+    } else {
+        const int orc = order_resident(L, stream);
+        if (orc) return orc;
+    }
     int rc = launch_forward(fp, T, stream);
     if (rc) {
         if (paged) L->mb_busy[slot].store(0);
@@ -1221,6 +1250,7 @@ int wisp_prefetch_async(wisp_layer *L, const int32_t *predicted, int32_t n, void
         if (rc) return rc;
     }
     WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
+    ++L->copy_gen;
     return WISP_OK;
 }
 
@@ -1249,6 +1279,7 @@ int wisp_prime_identity(wisp_layer *L, void *stream) {
     WISP_CUDA_TRY(cudaMemcpy(L->d_slot_ready, L->d_slot_gen, sizeof(uint32_t) * L->cap,
                              cudaMemcpyDeviceToDevice));
     WISP_CUDA_TRY(cudaEventRecord(L->ev_copies, L->copy_stream));
+    ++L->copy_gen;
     WISP_CUDA_TRY(cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(stream), L->ev_copies, 0));
     L->primed = true;
     return WISP_OK;
