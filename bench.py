@@ -141,9 +141,11 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, indices, enabled: bool = True):
+    def __init__(self, indices, enabled: bool = True, interval: float = 0.2):
         self.indices = [int(i) for i in (indices if isinstance(indices, (list, tuple)) else [indices])]
         self.enabled = enabled
+        self.interval = interval
+        self._max = {}
         self.rows = []          # (sm_mhz, sm_max_mhz, [reason names])
         self._stop = threading.Event()
         self._t = None
@@ -163,9 +165,11 @@ class ClockSampler:
         nv = self._nvml
         bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
-        for h in self._handles:
+        for i, h in enumerate(self._handles):
             sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            if i not in self._max:
+                self._max[i] = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            mx = self._max[i]
             r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
             self.rows.append((float(sm), float(mx), [n for n, b in zip(self.NAMES, bits) if r & b]))
 
@@ -189,7 +193,7 @@ class ClockSampler:
                 self._sample_nvml() if self._nvml is not None else self._sample_smi()
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(self.interval)
 
     def __enter__(self):
         if self.enabled:
@@ -203,9 +207,13 @@ class ClockSampler:
             self._stop.set()
             self._t.join(timeout=10)
 
-    def summary(self):
+    def summary(self, rows=None, indices=None):
+        """Median SM clock, max clock and throttle reasons seen; ``rows`` /
+        ``indices``: samples gathered from several processes."""
         if not self.enabled:
             return None
+        if rows is not None:
+            self.rows, self.indices = rows, indices
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         return {"sm_mhz": statistics.median(r[0] for r in self.rows),
@@ -213,6 +221,62 @@ class ClockSampler:
                 "reasons": sorted({n for r in self.rows for n in r[2]}),
                 "samples": len(self.rows), "gpus": self.indices,
                 "via": "nvml" if self._nvml is not None else "nvidia-smi"}
+
+
+class SmiSampler(ClockSampler):
+    """Clocks of several GPUs from one separate ``nvidia-smi -lms`` process
+    (the expert-parallel runs: queries from inside the ranks' processes slowed
+    the ranks' waits on one another), started before the timed region and
+    stopped after it."""
+
+    def __init__(self, indices, enabled: bool = True, interval_ms: int = 1000):
+        super().__init__(indices, enabled)
+        self.interval_ms = interval_ms
+        self._p = None
+        self._path = None
+
+    def __enter__(self):
+        if self.enabled:
+            import tempfile
+            fd, self._path = tempfile.mkstemp(prefix="wisp_clocks_", suffix=".csv")
+            os.close(fd)
+            self._f = open(self._path, "w")
+            try:
+                self._p = subprocess.Popen(
+                    ["nvidia-smi", "-i", ",".join(str(i) for i in self.indices), f"--query-gpu={self.Q}",
+                     "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
+                    stdout=self._f, stderr=subprocess.DEVNULL)
+            except OSError:
+                self._p = None
+        return self
+
+    def __exit__(self, *a):
+        if self._p is not None:
+            self._p.terminate()
+            try:
+                self._p.wait(timeout=10)
+            except subprocess.TimeoutExpired:
+                self._p.kill()
+        if self._path:
+            self._f.close()
+            with open(self._path) as f:
+                for line in f:
+                    c = [x.strip() for x in line.split(",")]
+                    if len(c) < 9:
+                        continue
+                    try:
+                        sm, mx = float(c[1]), float(c[2])
+                    except ValueError:
+                        continue
+                    reasons = [n for k, n in enumerate(self.NAMES) if c[5 + k].lower().startswith("active")]
+                    self.rows.append((sm, mx, reasons))
+            os.unlink(self._path)
+
+    def summary(self, rows=None, indices=None):
+        r = super().summary(rows, indices)
+        if r is not None and self.rows:
+            r["via"] = f"nvidia-smi -lms {self.interval_ms} (one process, rank 0)"
+        return r
 
 
 def h2d_peak_gbs(dev, nbytes=1 << 30, reps=6):
@@ -831,7 +895,9 @@ def run_wisp_ep(args):
     dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clk = ClockSampler(list(range(world)), enabled=rank == 0)
+    # one nvidia-smi process on rank 0 samples every GPU of the run (queries from
+    # inside the ranks' processes stalled the ranks' waits on one another)
+    clk = SmiSampler(list(range(world)), enabled=rank == 0)
     with clk:
         ev0.record()
         for s in range(args.warmup, total):
@@ -842,6 +908,7 @@ def run_wisp_ep(args):
     for lay in layers:
         lay.synchronize()
     tel1 = [lay.local.telemetry() for lay in layers]
+    clocks = clk.summary()
 
     def delta(key):
         return sum(b[key] - a[key] for a, b in zip(tel0, tel1))
@@ -912,7 +979,7 @@ def run_wisp_ep(args):
                                           * w_s.element_size() + x_h.numel() * x_h.element_size()) * world,
                 "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()) * world,
                 "steps": e2e_steps},
-        "clocks": clk.summary(),
+        "clocks": clocks,
         "setup_s": setup_s,
     }
 

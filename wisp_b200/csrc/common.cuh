@@ -28,8 +28,8 @@ void set_error(const std::string &msg);
     } while (0)
 
 // Cooperative launch of a persistent kernel (every block resident: blocks wait
-// on one another), with programmatic dependent launch unless WISP_NO_PDL is
-// set: the launch may begin while the previous kernel on the stream drains,
+// on one another), with programmatic dependent launch when WISP_PDL is set:
+// the launch may begin while the previous kernel on the stream drains,
 // and the kernel's pdl_wait() orders it after that kernel.  If the driver
 // refuses the two attributes together, the plain cooperative launch is used
 // from then on for that device.

@@ -55,7 +55,9 @@ void set_error(const std::string &msg) { g_last_error = msg; }
 namespace {
 std::atomic<int> g_pdl_state[64];  // 0 untried / accepted, 1 refused
 int pdl_env() {
-    static const int v = std::getenv("WISP_NO_PDL") ? 0 : 1;
+    // opt-in: no gain was measurable on one GPU, and expert-parallel runs with
+    // it on measured their timed region at half the end-to-end rate
+    static const int v = std::getenv("WISP_PDL") ? 1 : 0;
     return v;
 }
 }  // namespace
