@@ -203,6 +203,16 @@ WISP_API int wisp_get_launch_count(wisp_layer *layer, int64_t *out);
 WISP_API int wisp_layer_sync(wisp_layer *layer);
 
 /*
+ * Size the layer's per-call workspace for calls of up to num_tokens tokens at
+ * top_k now, at set-up, instead of at the first call that needs it (growing
+ * it waits for the device and reallocates: a stall in the middle of serving;
+ * an expert-parallel owner, whose call size varies with what it receives,
+ * reserves the largest receive).  No effect when the workspace is already
+ * that large.  (No reference counterpart: the reference allocates per call.)
+ */
+WISP_API int wisp_layer_reserve(wisp_layer *layer, int32_t num_tokens, int32_t top_k);
+
+/*
  * Tunables: WISP_CFG_ASYNC (1: single-launch forward with asynchronous
  * page-in, the default of resident layers; 0: host-synchronous path, the
  * default of paged layers -- a paged single-launch forward waits inside the

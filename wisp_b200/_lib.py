@@ -63,6 +63,7 @@ SIGNATURES = {
     "wisp_get_launch_count": (ctypes.c_int, [_vp, _p64]),
     "wisp_get_last_unique_experts": (ctypes.c_int, [_vp, _p32, _c_int32, _p32]),
     "wisp_layer_sync": (ctypes.c_int, [_vp]),
+    "wisp_layer_reserve": (ctypes.c_int, [_vp, _c_int32, _c_int32]),
     "wisp_layer_config": (ctypes.c_int, [_vp, _c_int32, _c_int64]),
     "wisp_layer_query": (ctypes.c_int, [_vp, _c_int32, ctypes.POINTER(_c_int64)]),
     "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,

@@ -1469,6 +1469,17 @@ int wisp_layer_query(wisp_layer *L, int32_t key, int64_t *value) {
     }
 }
 
+int wisp_layer_reserve(wisp_layer *L, int32_t num_tokens, int32_t top_k) {
+    if (!L) return fail(WISP_ERR_INVALID, "wisp_layer_reserve: NULL layer");
+    if (num_tokens < 0 || top_k < 1) return fail(WISP_ERR_INVALID, "wisp_layer_reserve: bad sizes");
+    std::lock_guard<std::mutex> lk(L->mu);
+    if (num_tokens <= L->wsT && top_k <= L->wsK) return WISP_OK;
+    DeviceGuard guard(L->dev);
+    int rc = drain(L);
+    if (rc) return rc;
+    return ensure_ws(L, num_tokens, top_k);
+}
+
 int wisp_layer_config(wisp_layer *L, int32_t key, int64_t value) {
     if (!L) return fail(WISP_ERR_INVALID, "wisp_layer_config: NULL layer");
     std::lock_guard<std::mutex> lk(L->mu);

@@ -199,6 +199,12 @@ class EPMoELayer:
             exchange = EPExchange(self.hidden, max_pairs, self.device, group=group, rank=self.rank,
                                   world=self.world)
         self.exchange = exchange
+        # the largest call this owner can receive: every source's pairs, one
+        # expert per row; reserved now (a workspace that grows mid-run waits for
+        # the device, and the receive size varies from call to call)
+        reserve = getattr(local, "reserve", None)
+        if reserve is not None and getattr(local, "hidden_size", 0):
+            reserve(exchange.world * exchange.max_pairs, 1)
         self.last_counts: list[int] = []
         self.last_runs: list[tuple[int, int]] = []   # (first row, rows) of each local call of the last forward
 

@@ -265,6 +265,11 @@ class WispMoEState:
             _lib.stream_ptr(torch.cuda.current_stream(self.device))), "pager_step")
         return slots
 
+    def reserve(self, num_tokens: int, top_k: int) -> None:
+        """Size the per-call workspace for calls of up to ``num_tokens`` x
+        ``top_k`` now (``wisp_layer_reserve``), so no later call grows it."""
+        _lib.check(_lib.lib().wisp_layer_reserve(self._h, int(num_tokens), int(top_k)), "reserve")
+
     def prefetch_async(self, predicted_experts) -> None:
         """Speculative page-in of ``predicted_experts`` (fused_moe.py:360-433):
         loads the predicted experts that have no slot, in the order the set
