@@ -244,3 +244,23 @@ def _mixed_worker(rank, world, port):
 
 def test_ep_mixed_call_sizes_gloo():
     mp.start_processes(_mixed_worker, args=(4, _free_port()), nprocs=4, start_method="spawn")
+
+
+def test_owner_reserves_its_largest_receive():
+    """An owner's call size is what it receives, which varies per call; its
+    layer reserves the largest receive (every source's pairs, one expert per
+    row) when built, so no call in a run grows the workspace."""
+    class _Reserving(_FakeExperts):
+        def __init__(self):
+            super().__init__(0, 4)
+            self.reserved = []
+
+        def reserve(self, num_tokens, top_k):
+            self.reserved.append((num_tokens, top_k))
+
+    class _Ex:
+        world, rank, hidden, max_pairs = 4, 1, H, 96
+
+    local = _Reserving()
+    EPMoELayer(None, None, 16, 4, local=local, device="cpu", exchange=_Ex())
+    assert local.reserved == [(4 * 96, 1)]
