@@ -207,13 +207,10 @@ class ClockSampler:
             self._stop.set()
             self._t.join(timeout=10)
 
-    def summary(self, rows=None, indices=None):
-        """Median SM clock, max clock and throttle reasons seen; ``rows`` /
-        ``indices``: samples gathered from several processes."""
+    def summary(self):
+        """Median SM clock, max clock and throttle reasons seen."""
         if not self.enabled:
             return None
-        if rows is not None:
-            self.rows, self.indices = rows, indices
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         return {"sm_mhz": statistics.median(r[0] for r in self.rows),
@@ -272,8 +269,8 @@ class SmiSampler(ClockSampler):
                     self.rows.append((sm, mx, reasons))
             os.unlink(self._path)
 
-    def summary(self, rows=None, indices=None):
-        r = super().summary(rows, indices)
+    def summary(self):
+        r = super().summary()
         if r is not None and self.rows:
             r["via"] = f"nvidia-smi -lms {self.interval_ms} (one process, rank 0)"
         return r
