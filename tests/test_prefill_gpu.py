@@ -110,3 +110,18 @@ def test_resident_prefill_routes_on_the_device():
     assert torch.equal(fwd(st, x, w, ids), out)
     assert st._read()[3] == [2, 0, 0, 0]
     st.close()
+
+
+@pytest.mark.parametrize("E,T,K,ids_dtype", [(1024, 300, 8, torch.int32), (64, 65, 8, torch.int64)])
+def test_resident_prefill_routing_edges(E, T, K, ids_dtype):
+    """The routing kernel at its expert limit (1024 experts, most with a few
+    pairs, one per thread of the block's scan) with int32 ids, and a call just
+    above the weight-stationary range (520 pairs: a few routing blocks)."""
+    H, I = 256, 128
+    w13, w2, x, w, ids = rand_case(E, H, I, T, K, seed=E + T)
+    st = state(w13, w2, E, "resident")
+    out = fwd(st, x, w, ids.to(ids_dtype))
+    c = compare(out, moe_reference(x, w13, w2, w, ids))
+    assert c["mean_rel"] <= MEAN_REL and c["max_abs"] <= MAX_ABS, c
+    assert st._read()[3] == [1, 0, 0, 0]
+    st.close()
