@@ -239,8 +239,12 @@ class SmiSampler(ClockSampler):
             os.close(fd)
             self._f = open(self._path, "w")
             try:
+                # nvidia-smi numbers the machine's GPUs; map the ranks' device
+                # indices through CUDA_VISIBLE_DEVICES when it is set
+                vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+                ids = [vis[i] if i < len(vis) else str(i) for i in self.indices]
                 self._p = subprocess.Popen(
-                    ["nvidia-smi", "-i", ",".join(str(i) for i in self.indices), f"--query-gpu={self.Q}",
+                    ["nvidia-smi", "-i", ",".join(ids), f"--query-gpu={self.Q}",
                      "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                     stdout=self._f, stderr=subprocess.DEVNULL)
             except OSError:
