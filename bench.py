@@ -156,7 +156,15 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
-            self._handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.indices]
+            # NVML numbers the machine's GPUs; map the CUDA device indices through
+            # CUDA_VISIBLE_DEVICES (indices or UUIDs) when it is set
+            vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+            hs = []
+            for i in self.indices:
+                v = vis[i] if i < len(vis) else str(i)
+                hs.append(pynvml.nvmlDeviceGetHandleByIndex(int(v)) if v.isdigit()
+                          else pynvml.nvmlDeviceGetHandleByUUID(v))
+            self._handles = hs
             self._nvml = pynvml
         except Exception:
             self._nvml = None
