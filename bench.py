@@ -182,8 +182,9 @@ class ClockSampler:
             self.rows.append((float(sm), float(mx), [n for n, b in zip(self.NAMES, bits) if r & b]))
 
     def _sample_smi(self):
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
         for i in self.indices:
-            out = subprocess.run(["nvidia-smi", "-i", str(i), f"--query-gpu={self.Q}",
+            out = subprocess.run(["nvidia-smi", "-i", vis[i] if i < len(vis) else str(i), f"--query-gpu={self.Q}",
                                   "--format=csv,noheader,nounits"], capture_output=True,
                                  text=True, timeout=5).stdout.strip()
             if not out:
