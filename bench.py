@@ -543,8 +543,8 @@ def sweep_phase(masters, dev, hbm_peak, h2d):
             # the reference's cross-layer prefetch on the B200 link (off by default
             # there too): a table learned online, warmed on 7 other steps of the
             # same routing process (same per-layer popularity, other draws)
-            from wisp_b200.integrations.vllm.cooccur import CooccurTable
-            table = CooccurTable()
+            from wisp_b200.integrations.vllm.cooccur import NativeCooccurTable
+            table = NativeCooccurTable()  # the plug-in's table
             wids, _ = wl.zipf_trace(12, L, B, q.experts, q.top_k, 1.1, 0.6, seed=11 + B)
             for s in range(5, 12):
                 table.observe_step({li: sorted(set(wids[s, li].reshape(-1).tolist())) for li in range(L)})

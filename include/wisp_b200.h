@@ -213,6 +213,34 @@ WISP_API int wisp_layer_sync(wisp_layer *layer);
 WISP_API int wisp_layer_reserve(wisp_layer *layer, int32_t num_tokens, int32_t top_k);
 
 /*
+ * Cross-layer co-activation table and prefetch predictor (host C++), the
+ * reference's CooccurTable / predict_layer (src/wisp/oracle/cooccur.py:44-292)
+ * with the same counts, scores (double, the reference's expression and
+ * accumulation order) and ranking (score descending, id ascending).  Layers
+ * and their experts are passed in CSR form: layers[i] with experts
+ * experts[offsets[i] .. offsets[i+1]), in the order the caller's dict holds
+ * them.  Export lists pairs [L_src, e_src, L_dst, e_dst, n] (n > 0) and
+ * marginals [L, e, n] in first-seen order (the reference's JSON schema).
+ */
+typedef struct wisp_cooccur wisp_cooccur;
+WISP_API int wisp_cooccur_create(wisp_cooccur **out);
+WISP_API int wisp_cooccur_destroy(wisp_cooccur *table);
+WISP_API int wisp_cooccur_observe_step(wisp_cooccur *table, int32_t n_layers, const int32_t *layers,
+                                       const int32_t *offsets, const int32_t *experts);
+WISP_API int wisp_cooccur_predict(const wisp_cooccur *table, int32_t n_seen, const int32_t *layers,
+                                  const int32_t *offsets, const int32_t *experts, int32_t target_layer, int32_t k,
+                                  int32_t normalize, double decay, int32_t only_prev_layer, int32_t *out_ids,
+                                  int32_t *n_out);
+WISP_API int wisp_cooccur_set_pair(wisp_cooccur *table, int32_t l_src, int32_t e_src, int32_t l_dst, int32_t e_dst,
+                                   int64_t n);
+WISP_API int wisp_cooccur_set_marginal(wisp_cooccur *table, int32_t l, int32_t e, int64_t n);
+WISP_API int wisp_cooccur_set_steps(wisp_cooccur *table, int64_t steps);
+WISP_API int wisp_cooccur_sizes(const wisp_cooccur *table, int64_t *n_sources, int64_t *n_pairs,
+                                int64_t *n_marginals, int64_t *steps);
+WISP_API int wisp_cooccur_export(const wisp_cooccur *table, int64_t *pairs, int64_t max_pairs, int64_t *n_pairs,
+                                 int64_t *marginals, int64_t max_marginals, int64_t *n_marginals);
+
+/*
  * Tunables: WISP_CFG_ASYNC (1: single-launch forward with asynchronous
  * page-in, the default of resident layers; 0: host-synchronous path, the
  * default of paged layers -- a paged single-launch forward waits inside the

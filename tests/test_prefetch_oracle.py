@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 from oracle.pager import PagerOracle, forward_pager
-from wisp_b200.integrations.vllm.cooccur import CooccurTable, predict_layer
+from wisp_b200.integrations.vllm.cooccur import CooccurTable, NativeCooccurTable, predict_layer
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "prefetch_golden.npz")
 
@@ -30,13 +30,16 @@ def unique_set(ids):
     return {int(e) for e in np.unique(np.asarray(ids)).tolist()}
 
 
+@pytest.mark.parametrize("table_cls", [CooccurTable, NativeCooccurTable], ids=["python", "native"])
 @pytest.mark.parametrize("name", sorted(CASES))
-def test_oracle_and_predictor_replay_reference_prefetch(name):
+def test_oracle_and_predictor_replay_reference_prefetch(name, table_cls):
+    """Both tables -- the Python restatement and the library's host C++ one
+    the plug-in uses -- issue the reference's predictions."""
     c = CASES[name]
     E, cap, L, S = int(c["E"]), int(c["cap"]), int(c["L"]), int(c["S"])
     pagers = [PagerOracle(E, cap) for _ in range(L)]
     last = [set() for _ in range(L)]
-    table, obs = CooccurTable(), {}
+    table, obs = table_cls(), {}
     f = 0
     for _s in range(S):
         for l in range(L):
@@ -87,3 +90,29 @@ def test_cooccur_table_schema_round_trip(tmp_path):
             {k: d[k] for k in ("schema_version", "num_steps_observed", "pairs", "marginals")}
     assert predict_layer(t, {0: {1}}, 2, k=2) == [5, 1]
     assert predict_layer(t, {}, 2) == []
+
+
+def test_native_table_matches_python_table():
+    """Random steps (layers in any order, empty layers, repeated ids): the same
+    serialisation, sizes and predictions under every predictor option."""
+    import random
+    rnd = random.Random(7)
+    py, nat = CooccurTable(), NativeCooccurTable()
+    L, E = 7, 24
+    for _ in range(40):
+        obs = {l: [rnd.randrange(E) for _ in range(rnd.randint(0, 6))]
+               for l in rnd.sample(range(L), rnd.randint(1, L))}
+        py.observe_step(obs)
+        nat.observe_step(obs)
+    assert py.to_dict() == nat.to_dict()
+    assert (py.n_source_keys, py.n_pairs, py.num_steps_observed) == \
+        (nat.n_source_keys, nat.n_pairs, nat.num_steps_observed)
+    for _ in range(300):
+        seen = {l: [rnd.randrange(E) for _ in range(rnd.randint(0, 6))]
+                for l in rnd.sample(range(L), rnd.randint(0, L))}
+        tgt = rnd.randrange(L + 1)
+        for kw in ({}, {"normalize": False}, {"decay": 0.5}, {"decay": 0.3, "only_prev_layer": True},
+                   {"k": 3, "decay": 0.7}):
+            assert predict_layer(py, seen, tgt, **kw) == predict_layer(nat, seen, tgt, **kw)
+    d = py.to_dict()
+    assert CooccurTable.from_dict(d).to_dict() == NativeCooccurTable.from_dict(d).to_dict()

@@ -64,6 +64,16 @@ SIGNATURES = {
     "wisp_get_last_unique_experts": (ctypes.c_int, [_vp, _p32, _c_int32, _p32]),
     "wisp_layer_sync": (ctypes.c_int, [_vp]),
     "wisp_layer_reserve": (ctypes.c_int, [_vp, _c_int32, _c_int32]),
+    "wisp_cooccur_create": (ctypes.c_int, [ctypes.POINTER(_vp)]),
+    "wisp_cooccur_destroy": (ctypes.c_int, [_vp]),
+    "wisp_cooccur_observe_step": (ctypes.c_int, [_vp, _c_int32, _p32, _p32, _p32]),
+    "wisp_cooccur_predict": (ctypes.c_int, [_vp, _c_int32, _p32, _p32, _p32, _c_int32, _c_int32, _c_int32,
+                                            ctypes.c_double, _c_int32, _p32, _p32]),
+    "wisp_cooccur_set_pair": (ctypes.c_int, [_vp, _c_int32, _c_int32, _c_int32, _c_int32, _c_int64]),
+    "wisp_cooccur_set_marginal": (ctypes.c_int, [_vp, _c_int32, _c_int32, _c_int64]),
+    "wisp_cooccur_set_steps": (ctypes.c_int, [_vp, _c_int64]),
+    "wisp_cooccur_sizes": (ctypes.c_int, [_vp, _p64, _p64, _p64, _p64]),
+    "wisp_cooccur_export": (ctypes.c_int, [_vp, _p64, _c_int64, _p64, _p64, _c_int64, _p64]),
     "wisp_layer_config": (ctypes.c_int, [_vp, _c_int32, _c_int64]),
     "wisp_layer_query": (ctypes.c_int, [_vp, _c_int32, ctypes.POINTER(_c_int64)]),
     "wisp_expert_compute_noalloc": (ctypes.c_int, [_c_int32, _vp, _vp, _vp, _c_int32, _vp, _vp,

@@ -105,11 +105,121 @@ class CooccurTable:
             return cls.from_dict(json.load(f))
 
 
-def predict_layer(table: CooccurTable, seen_so_far: Mapping[int, Iterable[int]], target_layer: int, *,
+def _csr(layers_map: Mapping[int, Iterable[int]]):
+    """{layer: experts} in its own order as ctypes CSR arrays (layers, offsets, experts)."""
+    import ctypes
+    ls, offs, es = [], [0], []
+    for L, xs in layers_map.items():
+        ls.append(int(L))
+        es.extend(int(e) for e in xs)
+        offs.append(len(es))
+    n = len(ls)
+    return (n, (ctypes.c_int32 * max(n, 1))(*ls), (ctypes.c_int32 * (n + 1))(*offs),
+            (ctypes.c_int32 * max(len(es), 1))(*es))
+
+
+class NativeCooccurTable:
+    """The same table in the library's host C++ (``wisp_cooccur_*``): the same
+    counts, serialisation order and scores as :class:`CooccurTable`, so the
+    same rankings, at native speed (the prediction walks every earlier layer's
+    experts once per layer of a decode step)."""
+
+    def __init__(self) -> None:
+        import ctypes
+        from wisp_b200 import _lib
+        self._lib = _lib
+        h = ctypes.c_void_p()
+        _lib.check(_lib.lib().wisp_cooccur_create(ctypes.byref(h)), "wisp_cooccur_create")
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                self._lib.lib().wisp_cooccur_destroy(h)
+            except Exception:  # interpreter shutdown: the library may be gone already
+                pass
+            self._h = None
+
+    def observe_step(self, expert_ids_by_layer: Mapping[int, Iterable[int]]) -> None:
+        n, ls, offs, es = _csr(expert_ids_by_layer)
+        self._lib.check(self._lib.lib().wisp_cooccur_observe_step(self._h, n, ls, offs, es),
+                        "wisp_cooccur_observe_step")
+
+    def predict(self, seen_so_far: Mapping[int, Iterable[int]], target_layer: int, *, k: int = 8,
+                normalize: bool = True, decay: float = 1.0, only_prev_layer: bool = False) -> list[int]:
+        import ctypes
+        n, ls, offs, es = _csr(seen_so_far)
+        out = (ctypes.c_int32 * max(int(k), 1))()
+        m = ctypes.c_int32(0)
+        self._lib.check(self._lib.lib().wisp_cooccur_predict(
+            self._h, n, ls, offs, es, int(target_layer), int(k), int(bool(normalize)), float(decay),
+            int(bool(only_prev_layer)), out, ctypes.byref(m)), "wisp_cooccur_predict")
+        return list(out[:m.value])
+
+    def _sizes(self):
+        import ctypes
+        v = [ctypes.c_int64(0) for _ in range(4)]
+        self._lib.check(self._lib.lib().wisp_cooccur_sizes(self._h, *[ctypes.byref(x) for x in v]),
+                        "wisp_cooccur_sizes")
+        return [x.value for x in v]
+
+    @property
+    def n_source_keys(self) -> int:
+        return self._sizes()[0]
+
+    @property
+    def n_pairs(self) -> int:
+        return self._sizes()[1]
+
+    @property
+    def num_steps_observed(self) -> int:
+        return self._sizes()[3]
+
+    def to_dict(self) -> dict:
+        import ctypes
+        n_src, n_pairs, n_marg, steps = self._sizes()
+        pairs = (ctypes.c_int64 * max(5 * n_pairs, 1))()
+        marg = (ctypes.c_int64 * max(3 * n_marg, 1))()
+        npo, nmo = ctypes.c_int64(0), ctypes.c_int64(0)
+        self._lib.check(self._lib.lib().wisp_cooccur_export(self._h, pairs, n_pairs, ctypes.byref(npo), marg,
+                                                             n_marg, ctypes.byref(nmo)), "wisp_cooccur_export")
+        P = [list(pairs[5 * i:5 * i + 5]) for i in range(npo.value)]
+        M = [list(marg[3 * i:3 * i + 3]) for i in range(nmo.value)]
+        return {"schema_version": SCHEMA_VERSION, "num_steps_observed": steps, "pairs": P, "marginals": M,
+                "stats": {"n_source_keys": n_src, "n_pairs": n_pairs, "memory_estimate_bytes": 40 * n_pairs}}
+
+    @classmethod
+    def from_dict(cls, data: Mapping) -> "NativeCooccurTable":
+        if int(data.get("schema_version", 1)) != SCHEMA_VERSION:
+            raise ValueError(f"cooccur table schema_version {data.get('schema_version')} unsupported")
+        t = cls()
+        L = t._lib.lib()
+        for L_src, e_src, L_dst, e_dst, n in data.get("pairs") or []:
+            t._lib.check(L.wisp_cooccur_set_pair(t._h, int(L_src), int(e_src), int(L_dst), int(e_dst), int(n)),
+                         "wisp_cooccur_set_pair")
+        for Lm, e, n in data.get("marginals") or []:
+            t._lib.check(L.wisp_cooccur_set_marginal(t._h, int(Lm), int(e), int(n)), "wisp_cooccur_set_marginal")
+        t._lib.check(L.wisp_cooccur_set_steps(t._h, int(data.get("num_steps_observed", 0))),
+                     "wisp_cooccur_set_steps")
+        return t
+
+    def save(self, path) -> None:
+        CooccurTable.from_dict(self.to_dict()).save(path)
+
+    @classmethod
+    def load(cls, path) -> "NativeCooccurTable":
+        return cls.from_dict(CooccurTable.load(path).to_dict())
+
+
+def predict_layer(table, seen_so_far: Mapping[int, Iterable[int]], target_layer: int, *,
                   k: int = 8, normalize: bool = True, decay: float = 1.0,
                   only_prev_layer: bool = False) -> list[int]:
     """Top-``k`` expert ids for ``target_layer`` given the experts seen at
     earlier layers of the current step; ``[]`` when nothing conditions."""
+    if isinstance(table, NativeCooccurTable):
+        return table.predict(seen_so_far, target_layer, k=k, normalize=normalize, decay=decay,
+                             only_prev_layer=only_prev_layer)
     scores: dict[int, float] = {}
     for L_src, src in seen_so_far.items():
         if L_src >= target_layer or (only_prev_layer and L_src != target_layer - 1):
@@ -128,4 +238,4 @@ def predict_layer(table: CooccurTable, seen_so_far: Mapping[int, Iterable[int]],
     return [e for e, _ in sorted(scores.items(), key=lambda kv: (-kv[1], kv[0]))[:k]]
 
 
-__all__ = ["CooccurTable", "predict_layer", "SCHEMA_VERSION"]
+__all__ = ["CooccurTable", "NativeCooccurTable", "predict_layer", "SCHEMA_VERSION"]

@@ -424,16 +424,19 @@ def _env_on(name: str) -> bool:
 def _maybe_load_cooccur():
     """The co-occurrence table: ``WISP_COOCCUR_PATH`` (a warm table in the
     reference's JSON schema) or a cold table when ``WISP_COOCCUR_ONLINE`` is
-    set; ``None`` when neither is configured (fused_moe.py:596-631)."""
+    set; ``None`` when neither is configured (fused_moe.py:596-631).  The
+    table lives in the library's host C++ (``NativeCooccurTable``: the same
+    counts and rankings as the reference's, at native speed)."""
     global _COOCCUR_TABLE
     if _COOCCUR_TABLE is not None:
         return _COOCCUR_TABLE or None
     path = os.environ.get("WISP_COOCCUR_PATH", "").strip()
     if not path and not _env_on("WISP_COOCCUR_ONLINE"):
         return None
-    from .cooccur import CooccurTable
+    from .cooccur import NativeCooccurTable
     try:
-        _COOCCUR_TABLE = CooccurTable.load(path) if path and os.path.isfile(path) else CooccurTable()
+        _COOCCUR_TABLE = (NativeCooccurTable.load(path) if path and os.path.isfile(path)
+                          else NativeCooccurTable())
     except Exception as e:
         logger.warning("wisp.vllm: cooccur table could not be loaded (%s); prefetch disabled", e)
         _COOCCUR_TABLE = False
