@@ -31,14 +31,19 @@
 #include "common.cuh"
 
 struct wisp_cooccur {
+    // One row (L_src, e_src) -> L_dst: entries in first-seen order (ids and
+    // counts apart, so a prediction streams them), and the same entries' indices
+    // sorted by id for the updates of observe_step (binary search).
     struct Row {
         int32_t l_dst;
-        std::vector<std::pair<int32_t, int64_t>> entries;  // (e_dst, n), first-seen order
-        std::unordered_map<int32_t, int32_t> pos;          // e_dst -> index in entries
+        std::vector<int32_t> ids;
+        std::vector<int64_t> n;
+        std::vector<int32_t> by_id;  // indices into ids, ascending by id
     };
     struct Source {
         int32_t l, e;
-        std::vector<Row> rows;  // first-seen order of L_dst
+        std::vector<Row> rows;         // first-seen order of L_dst
+        std::vector<int32_t> row_of;   // L_dst -> index + 1 into rows (0: none)
     };
     std::vector<Source> sources;                          // first-seen order of (L_src, e_src)
     std::unordered_map<int64_t, int32_t> source_of;       // (L, e) key -> index in sources
@@ -48,26 +53,45 @@ struct wisp_cooccur {
 
     static int64_t key(int32_t l, int32_t e) { return ((int64_t)l << 32) | (uint32_t)e; }
 
-    Source &source(int32_t l, int32_t e) {
+    int32_t source(int32_t l, int32_t e) {
         const int64_t k = key(l, e);
         auto it = source_of.find(k);
-        if (it != source_of.end()) return sources[it->second];
-        source_of.emplace(k, (int32_t)sources.size());
-        sources.push_back(Source{l, e, {}});
-        return sources.back();
+        if (it != source_of.end()) return it->second;
+        const int32_t i = (int32_t)sources.size();
+        source_of.emplace(k, i);
+        sources.push_back(Source{l, e, {}, {}});
+        return i;
     }
     static Row &row(Source &s, int32_t l_dst) {
-        for (Row &r : s.rows)
-            if (r.l_dst == l_dst) return r;
-        s.rows.push_back(Row{l_dst, {}, {}});
+        if (l_dst >= 0 && (size_t)l_dst < s.row_of.size() && s.row_of[l_dst]) return s.rows[s.row_of[l_dst] - 1];
+        if (l_dst >= 0) {
+            if ((size_t)l_dst >= s.row_of.size()) s.row_of.resize((size_t)l_dst + 1, 0);
+            s.row_of[l_dst] = (int32_t)s.rows.size() + 1;
+        } else {
+            for (Row &r : s.rows)  // negative layer ids: no index, a scan
+                if (r.l_dst == l_dst) return r;
+        }
+        s.rows.push_back(Row{l_dst, {}, {}, {}});
         return s.rows.back();
     }
+    static const Row *find_row(const Source &s, int32_t l_dst) {
+        if (l_dst >= 0) {
+            if ((size_t)l_dst < s.row_of.size() && s.row_of[l_dst]) return &s.rows[s.row_of[l_dst] - 1];
+            return nullptr;
+        }
+        for (const Row &r : s.rows)
+            if (r.l_dst == l_dst) return &r;
+        return nullptr;
+    }
     static int64_t &entry(Row &r, int32_t e_dst) {
-        auto it = r.pos.find(e_dst);
-        if (it != r.pos.end()) return r.entries[it->second].second;
-        r.pos.emplace(e_dst, (int32_t)r.entries.size());
-        r.entries.emplace_back(e_dst, 0);
-        return r.entries.back().second;
+        auto it = std::lower_bound(r.by_id.begin(), r.by_id.end(), e_dst,
+                                   [&](int32_t idx, int32_t v) { return r.ids[idx] < v; });
+        if (it != r.by_id.end() && r.ids[*it] == e_dst) return r.n[*it];
+        const int32_t idx = (int32_t)r.ids.size();
+        r.ids.push_back(e_dst);
+        r.n.push_back(0);
+        r.by_id.insert(it, idx);
+        return r.n.back();
     }
     int64_t &marginal(int32_t l, int32_t e) {
         const int64_t k = key(l, e);
@@ -124,8 +148,7 @@ int wisp_cooccur_observe_step(wisp_cooccur *t, int32_t n_layers, const int32_t *
     for (int32_t i : live) {
         for (int32_t j = offsets[i]; j < offsets[i + 1]; ++j) {
             // the source's entry exists from its first observation on (even with no later layer)
-            t->source(layers[i], experts[j]);
-            const int32_t si = t->source_of[wisp_cooccur::key(layers[i], experts[j])];
+            const int32_t si = t->source(layers[i], experts[j]);
             for (int32_t d : live) {
                 if (layers[d] <= layers[i]) continue;
                 wisp_cooccur::Row &r = wisp_cooccur::row(t->sources[si], layers[d]);
@@ -142,7 +165,9 @@ int wisp_cooccur_predict(const wisp_cooccur *t, int32_t n_seen, const int32_t *l
                          int32_t only_prev_layer, int32_t *out_ids, int32_t *n_out) {
     if (!t || !n_out || k < 0 || (k > 0 && !out_ids) || bad_csr(n_seen, layers, offsets, experts))
         return set_error("wisp_cooccur_predict: bad arguments"), WISP_ERR_INVALID;
-    std::unordered_map<int32_t, double> score;
+    // dense scores over the expert ids seen (a flag marks the scored ones)
+    std::vector<double> score;
+    std::vector<char> scored;
     std::vector<int32_t> order;  // experts with a score (any order: the ranking breaks ties by id)
     for (int32_t i = 0; i < n_seen; ++i) {
         const int32_t l_src = layers[i];
@@ -151,26 +176,31 @@ int wisp_cooccur_predict(const wisp_cooccur *t, int32_t n_seen, const int32_t *l
         for (int32_t j = offsets[i]; j < offsets[i + 1]; ++j) {
             const wisp_cooccur::Source *s = t->find_source(l_src, experts[j]);
             if (!s) continue;
-            const wisp_cooccur::Row *r = nullptr;
-            for (const auto &x : s->rows)
-                if (x.l_dst == target_layer) r = &x;
-            if (!r || r->entries.empty()) continue;
+            const wisp_cooccur::Row *r = wisp_cooccur::find_row(*s, target_layer);
+            if (!r || r->ids.empty()) continue;
             const int64_t total = normalize ? t->marginal_or_zero(l_src, experts[j]) : 1;
             const double denom = (normalize && total > 0) ? (double)total : 1.0;
-            for (const auto &en : r->entries) {
-                auto it = score.find(en.first);
-                const double add = w * (double)en.second / denom;
-                if (it == score.end()) {
-                    score.emplace(en.first, 0.0 + add);
-                    order.push_back(en.first);
+            const size_t ne = r->ids.size();
+            for (size_t q = 0; q < ne; ++q) {
+                const double add = w * (double)r->n[q] / denom;
+                const int32_t id = r->ids[q];
+                const size_t e = (size_t)(uint32_t)id;
+                if (e >= score.size()) {
+                    score.resize(e + 1, 0.0);
+                    scored.resize(e + 1, 0);
+                }
+                if (!scored[e]) {
+                    scored[e] = 1;
+                    score[e] = 0.0 + add;
+                    order.push_back(id);
                 } else {
-                    it->second = it->second + add;
+                    score[e] = score[e] + add;
                 }
             }
         }
     }
     std::sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
-        const double sa = score[a], sb = score[b];
+        const double sa = score[(uint32_t)a], sb = score[(uint32_t)b];
         return sa != sb ? sa > sb : a < b;
     });
     const int32_t n = std::min<int32_t>(k, (int32_t)order.size());
@@ -181,7 +211,8 @@ int wisp_cooccur_predict(const wisp_cooccur *t, int32_t n_seen, const int32_t *l
 
 int wisp_cooccur_set_pair(wisp_cooccur *t, int32_t l_src, int32_t e_src, int32_t l_dst, int32_t e_dst, int64_t n) {
     if (!t) return set_error("wisp_cooccur_set_pair: NULL table"), WISP_ERR_INVALID;
-    wisp_cooccur::entry(wisp_cooccur::row(t->source(l_src, e_src), l_dst), e_dst) = n;
+    const int32_t si = t->source(l_src, e_src);
+    wisp_cooccur::entry(wisp_cooccur::row(t->sources[si], l_dst), e_dst) = n;
     return WISP_OK;
 }
 
@@ -202,7 +233,7 @@ int wisp_cooccur_sizes(const wisp_cooccur *t, int64_t *n_sources, int64_t *n_pai
     if (!t) return set_error("wisp_cooccur_sizes: NULL table"), WISP_ERR_INVALID;
     int64_t pairs = 0;
     for (const auto &s : t->sources)
-        for (const auto &r : s.rows) pairs += (int64_t)r.entries.size();
+        for (const auto &r : s.rows) pairs += (int64_t)r.ids.size();
     if (n_sources) *n_sources = (int64_t)t->sources.size();
     if (n_pairs) *n_pairs = pairs;
     if (n_marginals) *n_marginals = (int64_t)t->marginals.size();
@@ -217,15 +248,15 @@ int wisp_cooccur_export(const wisp_cooccur *t, int64_t *pairs, int64_t max_pairs
     int64_t np = 0, nm = 0;
     for (const auto &s : t->sources)
         for (const auto &r : s.rows)
-            for (const auto &en : r.entries) {
-                if (en.second <= 0) continue;
+            for (size_t q = 0; q < r.ids.size(); ++q) {
+                if (r.n[q] <= 0) continue;
                 if (np < max_pairs) {
                     int64_t *p = pairs + 5 * np;
                     p[0] = s.l;
                     p[1] = s.e;
                     p[2] = r.l_dst;
-                    p[3] = en.first;
-                    p[4] = en.second;
+                    p[3] = r.ids[q];
+                    p[4] = r.n[q];
                 }
                 ++np;
             }
